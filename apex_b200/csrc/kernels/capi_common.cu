@@ -1,0 +1,138 @@
+// capi_common.cu -- error reporting, device status word, SM count and tensor-map encoding
+// shared by every C-ABI entry point.
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace apex {
+
+// One status word per device, written by kernels whose bounded waits give up (they receive
+// its address) and read and cleared by apex_cuda_device_status.
+static __device__ unsigned int g_device_status = 0;
+
+namespace {
+thread_local std::string t_last_error;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+}  // namespace
+
+int fail(int code, const std::string &msg) {
+    t_last_error = msg;
+    return code;
+}
+
+int check_cuda(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return APEX_OK;
+    return fail(APEX_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int ok() {
+    t_last_error.clear();
+    return APEX_OK;
+}
+
+int sm_count() {
+    static std::mutex mu;
+    static std::vector<int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    std::lock_guard<std::mutex> lock(mu);
+    if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
+    if (cache[dev] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
+}
+
+unsigned *device_status_ptr() {
+    static std::mutex mu;
+    static std::vector<unsigned *> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if ((int)cache.size() <= dev) cache.resize(dev + 1, nullptr);
+    if (!cache[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+        cache[dev] = static_cast<unsigned *>(p);
+    }
+    return cache[dev];
+}
+
+int make_tensor_map_bf16_3d(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1,
+                            uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                            uint32_t box0, uint32_t box1) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(APEX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    const cuuint32_t box[3] = {box0, box1, 1};
+    const cuuint32_t estride[3] = {1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims,
+                          strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(APEX_ERR_INVALID_ARGUMENT,
+                    "cuTensorMapEncodeTiled rejected the tensor (error " + std::to_string((int)r) +
+                        "): base must be 16-byte aligned and strides multiples of 16 bytes");
+    return APEX_OK;
+}
+
+}  // namespace apex
+
+extern "C" {
+
+const char *apex_cuda_last_error(void) { return apex::t_last_error.c_str(); }
+
+int apex_cuda_abi_version(void) { return 100; }
+
+int apex_cuda_device_status(void *stream) {
+    unsigned int host = 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int rc = apex::check_cuda(
+        cudaMemcpyFromSymbolAsync(&host, apex::g_device_status, sizeof(host), 0,
+                                  cudaMemcpyDeviceToHost, s),
+        "read device status");
+    if (rc) return rc;
+    rc = apex::check_cuda(cudaStreamSynchronize(s), "synchronize");
+    if (rc) return rc;
+    if (host) {
+        const unsigned int zero = 0;
+        rc = apex::check_cuda(cudaMemcpyToSymbolAsync(apex::g_device_status, &zero, sizeof(zero), 0,
+                                                      cudaMemcpyHostToDevice, s),
+                              "clear device status");
+        if (rc) return rc;
+        rc = apex::check_cuda(cudaStreamSynchronize(s), "synchronize");
+        if (rc) return rc;
+        if (host & apex::kStatusTimeout)
+            return apex::fail(APEX_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait gave up");
+        return apex::fail(APEX_ERR_INVALID_ARGUMENT,
+                          "a kernel skipped a sequence whose length exceeded max_seq_len or the cache");
+    }
+    return apex::ok();
+}
+
+}  // extern "C"

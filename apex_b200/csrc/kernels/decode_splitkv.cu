@@ -1,0 +1,595 @@
+// decode_splitkv.cu -- fused single-token decode over a bf16 KV cache (split-KV), plus the
+// log-sum-exp merge of per-GPU partials.
+//
+// Reference semantics: the new token's q is normalised and roped (shaders/head_norm_rope.metal,
+// called on q at docs/B6_3_attention.md:445-446), its k/v are normalised (k also roped) and
+// written into the cache at position L-1 (docs/B6_3_attention.md:448-452), then the softmax
+// over the visible keys is taken per q head with the GQA map h / (Hq/Hkv) and the window rule
+// (attention_f32, docs/B6_3_attention.md:296-343).  Decode is T = 1 of that same kernel
+// (docs/B6_3_attention.md:95-97).
+//
+// B200 design (HBM-bound): work item = (sequence b, kv head, split of `chunk` positions).
+// One CTA = 4 consumer warps + 1 producer warp.  The producer streams contiguous runs of K
+// and V rows ([pos][256] bf16, 512 B each) with 1-D TMA bulk copies into a 3-stage ring of
+// 32 positions (16 KB K + 16 KB V per stage), so every byte of the cache is read once, in
+// 16 KB bursts, by the copy engine.  Each consumer warp owns 8 positions of a stage and keeps
+// a private online softmax for BOTH q heads of the GQA group (the K/V row is read once for
+// both): lane l holds dims [8l, 8l+8) of q and of the accumulators; one 128-bit shared load
+// per lane reads a whole 512 B row; the 16 partial dot products (8 positions x 2 heads) are
+// reduced with a 16-shuffle transposed butterfly that leaves one finished score per lane.
+// Scores live in the log2 domain (q is pre-scaled by scale*log2(e)), so exponentials are
+// single ex2 instructions.  Warps merge once per CTA; the last CTA of each (b, kv head)
+// (atomic counter, no spin) merges the split partials and writes bf16 -- one launch per step.
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+#include "row256.cuh"
+
+namespace apex {
+namespace {
+
+constexpr int kD = 256;                 // head_dim
+constexpr int kG = 2;                   // q heads per kv head (GQA group)
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStagePos = 32;
+constexpr int kStages = 3;
+constexpr int kRowBytes = kD * 2;
+constexpr int kStageBytes = kStagePos * kRowBytes;
+constexpr int kPosPerWarp = kStagePos / kConsumerWarps;
+constexpr int kPart = kD + 2;           // public partial record: o[D], m, l
+constexpr int kWsRec = kD + 4;          // workspace record: o[D], m, l, pad (16-byte multiple)
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct DecodeArgs {
+    const uint16_t *q_raw, *k_new, *v_new, *q_w, *k_w;
+    uint16_t *k_cache, *v_cache;
+    const int32_t *seq_lens;
+    uint16_t *out;       // [B][Hq][D] bf16 (full mode)
+    float *partial_out;  // [B][Hq][D+2]   (partial mode)
+    float *ws_part;      // [B][Hq][max_splits][D+4]
+    unsigned *ws_count;  // [B][Hkv]
+    unsigned *status;    // device status word
+    uint32_t capacity, q_heads, kv_heads, rope_pairs, window, qk_norm, v_norm;
+    uint32_t chunk, max_splits, kv_begin, kv_end, max_seq_len;
+    float rope_base, eps, scale_log2;
+    int partial_mode;
+};
+
+struct __align__(16) DecodeSmem {
+    uint8_t k[kStages][kStageBytes];
+    uint8_t v[kStages][kStageBytes];
+    float q[kG][kD];
+    uint16_t new_k[kD];
+    uint16_t new_v[kD];
+    float inv_freq[kD / 2];
+    float wm[kConsumerWarps][kG], wl[kConsumerWarps][kG];
+    uint64_t full[kStages], empty[kStages];
+    int is_last;
+};
+
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+}
+
+// Online-softmax update of one warp with up to 8 key/value rows (row j at kbase/vbase +
+// j*512 bytes in shared memory).  State: m[g] (log2 units, warp-uniform), lpart (this lane's
+// share of l for head (lane>>1)&1), acc[g][8] (dims [8l, 8l+8) of head g).
+__device__ __forceinline__ void warp_step(const uint8_t *kbase, const uint8_t *vbase, int nvalid,
+                                          uint32_t lane, const float (&qf)[kG][8],
+                                          float (&m)[kG], float &lpart, float (&acc)[kG][8]) {
+    float part[16];
+#pragma unroll
+    for (int j = 0; j < kPosPerWarp; ++j) {
+        if (j < nvalid) {
+            const uint4 raw = *reinterpret_cast<const uint4 *>(kbase + j * kRowBytes + lane * 16);
+            float kf[8];
+            unpack8(raw, kf);
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                s0 = fmaf(qf[0][e], kf[e], s0);
+                s1 = fmaf(qf[1][e], kf[e], s1);
+            }
+            part[2 * j] = s0;
+            part[2 * j + 1] = s1;
+        } else {
+            part[2 * j] = 0.f;
+            part[2 * j + 1] = 0.f;
+        }
+    }
+    // Transposed butterfly: after the 5 rounds lane l holds the full score of value index
+    // l >> 1 = 2*j + g, i.e. position j = l >> 2 and head g = (l >> 1) & 1.
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+    float r1[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float keep = b4 ? part[i + 8] : part[i];
+        const float send = b4 ? part[i] : part[i + 8];
+        r1[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+    float r2[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float keep = b3 ? r1[i + 4] : r1[i];
+        const float send = b3 ? r1[i] : r1[i + 4];
+        r2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    float r3[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float keep = b2 ? r2[i + 2] : r2[i];
+        const float send = b2 ? r2[i] : r2[i + 2];
+        r3[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    float s = (b1 ? r3[1] : r3[0]) + __shfl_xor_sync(0xffffffffu, b1 ? r3[0] : r3[1], 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    const int my_j = lane >> 2;
+    const int my_g = (lane >> 1) & 1;
+    if (my_j >= nvalid) s = -INFINITY;
+
+    float mx = s;
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float mo = __shfl_xor_sync(0xffffffffu, mx, 2);
+    float m_new[kG], alpha[kG];
+    m_new[0] = fmaxf(m[0], my_g == 0 ? mx : mo);
+    m_new[1] = fmaxf(m[1], my_g == 0 ? mo : mx);
+#pragma unroll
+    for (int g = 0; g < kG; ++g) alpha[g] = fast_exp2(m[g] - m_new[g]);  // 0 when m = -inf
+    const float p = fast_exp2(s - m_new[my_g]);                          // 0 for invalid rows
+    lpart = lpart * alpha[my_g] + p;
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[g][e] *= alpha[g];
+        m[g] = m_new[g];
+    }
+    for (int j = 0; j < nvalid; ++j) {
+        const float p0 = __shfl_sync(0xffffffffu, p, 4 * j);
+        const float p1 = __shfl_sync(0xffffffffu, p, 4 * j + 2);
+        const uint4 raw = *reinterpret_cast<const uint4 *>(vbase + j * kRowBytes + lane * 16);
+        float vf[8];
+        unpack8(raw, vf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            acc[0][e] = fmaf(p0, vf[e], acc[0][e]);
+            acc[1][e] = fmaf(p1, vf[e], acc[1][e]);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const DecodeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    DecodeSmem &sm = *reinterpret_cast<DecodeSmem *>(smem_raw);
+
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const uint32_t Hq = a.q_heads;
+
+    // ---- key range of this (b, kv head) and of this split (global positions)
+    const int32_t L = a.seq_lens[b];
+    const bool bad = L < 0 || static_cast<uint32_t>(L) > a.max_seq_len ||
+                     (L > 0 && static_cast<uint32_t>(L) - 1 >= a.kv_begin + a.capacity &&
+                      static_cast<uint32_t>(L) - 1 < a.kv_end);
+    const uint32_t Lu = bad ? 0u : static_cast<uint32_t>(L);
+    const uint32_t pos_new = Lu - 1;  // only meaningful when Lu >= 1
+    const uint32_t first = (a.window && Lu > a.window) ? Lu - a.window : 0;
+    const uint32_t kb = max(first, a.kv_begin);
+    const uint32_t ke = min(Lu, a.kv_end);
+    const uint32_t n_keys = ke > kb ? ke - kb : 0;
+    const uint32_t nsplit = n_keys ? (n_keys + a.chunk - 1) / a.chunk : 1;
+    if (bad && split == 0 && tid == 0 && kvh == 0) atomicOr(a.status, kStatusBadLength);
+    if (split >= nsplit) return;
+    if (nsplit > a.max_splits) {  // cannot happen for lengths <= max_seq_len
+        if (tid == 0) atomicOr(a.status, kStatusBadLength);
+        return;
+    }
+    const uint32_t lo = kb + split * a.chunk;
+    const uint32_t hi = n_keys ? min(lo + a.chunk, ke) : lo;
+    const bool has_new = n_keys && pos_new >= lo && pos_new < hi;
+    const uint32_t cache_hi = has_new ? pos_new : hi;
+    const uint32_t n_cached = cache_hi > lo ? cache_hi - lo : 0;
+    const uint32_t n_stages = (n_cached + kStagePos - 1) / kStagePos;
+
+    const uint64_t head_base =
+        (static_cast<uint64_t>(b) * a.kv_heads + kvh) * a.capacity * kD;  // element offset
+    const uint16_t *kc = a.k_cache + head_base + static_cast<uint64_t>(lo - a.kv_begin) * kD;
+    const uint16_t *vc = a.v_cache + head_base + static_cast<uint64_t>(lo - a.kv_begin) * kD;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_u32(&sm.full[s]), 1);
+            mbar_init(smem_u32(&sm.empty[s]), kConsumerWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ---------------------------------------------------------------- producer
+        if (lane == 0) {
+            for (uint32_t s = 0; s < n_stages; ++s) {
+                const uint32_t slot = s % kStages;
+                if (s >= kStages && !mbar_wait(smem_u32(&sm.empty[slot]), ((s / kStages) - 1) & 1, a.status))
+                    break;
+                const uint32_t p0 = s * kStagePos;
+                const uint32_t n = min(static_cast<uint32_t>(kStagePos), n_cached - p0);
+                const uint32_t bytes = n * kRowBytes;
+                const uint32_t full = smem_u32(&sm.full[slot]);
+                mbar_arrive_expect_tx(full, 2 * bytes);
+                tma_bulk_load(smem_u32(sm.k[slot]), kc + static_cast<uint64_t>(p0) * kD, bytes, full);
+                tma_bulk_load(smem_u32(sm.v[slot]), vc + static_cast<uint64_t>(p0) * kD, bytes, full);
+            }
+        }
+        return;
+    }
+
+    // -------------------------------------------------------------------- consumers
+    for (uint32_t i = tid; i < a.rope_pairs; i += kConsumerWarps * 32)
+        sm.inv_freq[i] = rope_inv_freq(i, kD, a.rope_base);
+    consumer_sync();
+    const float pos_f = static_cast<float>(pos_new);
+    if (warp < kG) {
+        // q of head kvh*G + warp: norm + rope at the new position, pre-scaled for exp2.
+        const uint32_t h = kvh * kG + warp;
+        const uint4 raw = *reinterpret_cast<const uint4 *>(
+            a.q_raw + (static_cast<uint64_t>(b) * Hq + h) * kD + 8 * lane);
+        float x[8];
+        unpack8(raw, x);
+        norm_rope_row(x, lane, a.qk_norm, a.q_w, a.eps, a.rope_pairs, sm.inv_freq, pos_f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sm.q[warp][8 * lane + e] = x[e] * a.scale_log2;
+    } else if (has_new) {
+        // new k (warp 2): norm + rope; new v (warp 3): optional weightless norm.  Both are
+        // rounded to bf16 once, stored to the cache and kept in shared memory for this split.
+        const bool is_k = warp == kG;
+        const uint16_t *src = (is_k ? a.k_new : a.v_new) + (static_cast<uint64_t>(b) * a.kv_heads + kvh) * kD;
+        const uint4 raw = *reinterpret_cast<const uint4 *>(src + 8 * lane);
+        float x[8];
+        unpack8(raw, x);
+        if (is_k)
+            norm_rope_row(x, lane, a.qk_norm, a.k_w, a.eps, a.rope_pairs, sm.inv_freq, pos_f);
+        else
+            norm_rope_row(x, lane, a.v_norm, nullptr, a.eps, 0, sm.inv_freq, pos_f);
+        const uint4 packed = pack8(x);
+        *reinterpret_cast<uint4 *>((is_k ? sm.new_k : sm.new_v) + 8 * lane) = packed;
+        uint16_t *dst = (is_k ? a.k_cache : a.v_cache) + head_base +
+                        static_cast<uint64_t>(pos_new - a.kv_begin) * kD;
+        *reinterpret_cast<uint4 *>(dst + 8 * lane) = packed;
+    }
+    consumer_sync();
+
+    float qf[kG][8];
+#pragma unroll
+    for (int g = 0; g < kG; ++g)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) qf[g][e] = sm.q[g][8 * lane + e];
+
+    float m[kG] = {-INFINITY, -INFINITY};
+    float lpart = 0.f;
+    float acc[kG][8];
+#pragma unroll
+    for (int g = 0; g < kG; ++g)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
+
+    for (uint32_t s = 0; s < n_stages; ++s) {
+        const uint32_t slot = s % kStages;
+        if (!mbar_wait(smem_u32(&sm.full[slot]), (s / kStages) & 1, a.status)) break;
+        const int n = static_cast<int>(min(static_cast<uint32_t>(kStagePos), n_cached - s * kStagePos));
+        const int nvalid = min(max(n - static_cast<int>(warp) * kPosPerWarp, 0), kPosPerWarp);
+        if (nvalid > 0)
+            warp_step(sm.k[slot] + warp * kPosPerWarp * kRowBytes,
+                      sm.v[slot] + warp * kPosPerWarp * kRowBytes, nvalid, lane, qf, m, lpart, acc);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sm.empty[slot]));
+    }
+    if (has_new && warp == 0)
+        warp_step(reinterpret_cast<const uint8_t *>(sm.new_k),
+                  reinterpret_cast<const uint8_t *>(sm.new_v), 1, lane, qf, m, lpart, acc);
+
+    // ---- per-warp l: sum this lane's share over the 8 positions of its head
+    float lt = lpart;
+    lt += __shfl_xor_sync(0xffffffffu, lt, 4);
+    lt += __shfl_xor_sync(0xffffffffu, lt, 8);
+    lt += __shfl_xor_sync(0xffffffffu, lt, 16);
+    const float lother = __shfl_xor_sync(0xffffffffu, lt, 2);
+    const int my_g = (lane >> 1) & 1;
+    consumer_sync();  // every warp is done with the stage buffers: reuse them for the merge
+    float *wacc = reinterpret_cast<float *>(sm.k[0]);  // [warps][G][D] f32 = 8 KB
+    if (lane == 0) {
+        sm.wm[warp][0] = m[0];
+        sm.wm[warp][1] = m[1];
+        sm.wl[warp][0] = my_g == 0 ? lt : lother;
+        sm.wl[warp][1] = my_g == 0 ? lother : lt;
+    }
+#pragma unroll
+    for (int g = 0; g < kG; ++g)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) wacc[(warp * kG + g) * kD + 8 * lane + e] = acc[g][e];
+    consumer_sync();
+
+    // ---- CTA merge: thread t owns head g = t / 64, dims [4*(t%64), +4)
+    const uint32_t g = tid / 64, d0 = (tid % 64) * 4;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w)
+        if (sm.wl[w][g] > 0.f) M = fmaxf(M, sm.wm[w][g]);
+    float den = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+        if (!(sm.wl[w][g] > 0.f)) continue;
+        const float wt = fast_exp2(sm.wm[w][g] - M);
+        den += wt * sm.wl[w][g];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] += wt * wacc[(w * kG + g) * kD + d0 + e];
+    }
+    const float inv_den = den > 0.f ? 1.0f / den : 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] *= inv_den;
+    const uint32_t h = kvh * kG + g;
+    const uint64_t row = static_cast<uint64_t>(b) * Hq + h;
+
+    if (nsplit == 1) {
+        if (a.partial_mode) {
+            float *dst = a.partial_out + row * kPart;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[d0 + e] = o[e];
+            if (d0 == 0) {
+                dst[kD] = M;
+                dst[kD + 1] = den;
+            }
+        } else {
+            uint2 packed;
+            packed.x = pack_bf16(o[0], o[1]);
+            packed.y = pack_bf16(o[2], o[3]);
+            *reinterpret_cast<uint2 *>(a.out + row * kD + d0) = packed;
+        }
+        return;
+    }
+
+    // ---- split partial -> workspace; the last CTA of (b, kv head) merges all splits
+    float *mine = a.ws_part + (row * a.max_splits + split) * kWsRec;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) mine[d0 + e] = o[e];
+    if (d0 == 0) {
+        mine[kD] = M;
+        mine[kD + 1] = den;
+    }
+    __threadfence();
+    consumer_sync();
+    if (tid == 0) {
+        unsigned *counter = a.ws_count + static_cast<uint64_t>(b) * a.kv_heads + kvh;
+        const unsigned prev = atomicAdd(counter, 1u);
+        const int last = prev == nsplit - 1;
+        if (last) *counter = 0;  // ready for the next call
+        sm.is_last = last;
+    }
+    consumer_sync();
+    if (!sm.is_last) return;
+    __threadfence();
+    const float *parts = a.ws_part + row * a.max_splits * kWsRec;
+    float Mx = -INFINITY;
+    for (uint32_t s = 0; s < nsplit; ++s) {
+        const float l_s = __ldcg(parts + s * kWsRec + kD + 1);
+        if (l_s > 0.f) Mx = fmaxf(Mx, __ldcg(parts + s * kWsRec + kD));
+    }
+    float dsum = 0.f, r[4] = {0.f, 0.f, 0.f, 0.f};
+    for (uint32_t s = 0; s < nsplit; ++s) {
+        const float *p = parts + s * kWsRec;
+        const float l_s = __ldcg(p + kD + 1);
+        if (!(l_s > 0.f)) continue;
+        const float wt = fast_exp2(__ldcg(p + kD) - Mx) * l_s;
+        dsum += wt;
+        const float4 ov = __ldcg(reinterpret_cast<const float4 *>(p + d0));
+        r[0] += wt * ov.x;
+        r[1] += wt * ov.y;
+        r[2] += wt * ov.z;
+        r[3] += wt * ov.w;
+    }
+    const float inv = dsum > 0.f ? 1.0f / dsum : 0.f;
+    if (a.partial_mode) {
+        // A rank partial stores l relative to its own max Mx: l_rank = sum_s 2^(m_s - Mx) l_s.
+        float *dst = a.partial_out + row * kPart;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dst[d0 + e] = r[e] * inv;
+        if (d0 == 0) {
+            dst[kD] = Mx;
+            dst[kD + 1] = dsum;
+        }
+    } else {
+        uint2 packed;
+        packed.x = pack_bf16(r[0] * inv, r[1] * inv);
+        packed.y = pack_bf16(r[2] * inv, r[3] * inv);
+        *reinterpret_cast<uint2 *>(a.out + row * kD + d0) = packed;
+    }
+}
+
+__global__ void merge_partials_kernel(const float *__restrict__ parts, uint32_t num_parts,
+                                      uint32_t rows, uint32_t head_dim, uint16_t *__restrict__ out) {
+    const uint32_t row = blockIdx.x;
+    const uint64_t rec = head_dim + 2;
+    float M = -INFINITY;
+    for (uint32_t r = 0; r < num_parts; ++r) {
+        const float *p = parts + (static_cast<uint64_t>(r) * rows + row) * rec;
+        if (p[head_dim + 1] > 0.f) M = fmaxf(M, p[head_dim]);
+    }
+    for (uint32_t d = threadIdx.x; d < head_dim; d += blockDim.x) {
+        float den = 0.f, num = 0.f;
+        for (uint32_t r = 0; r < num_parts; ++r) {
+            const float *p = parts + (static_cast<uint64_t>(r) * rows + row) * rec;
+            const float l = p[head_dim + 1];
+            if (!(l > 0.f)) continue;
+            const float wt = fast_exp2(p[head_dim] - M) * l;
+            den += wt;
+            num += wt * p[d];
+        }
+        __nv_bfloat16 v = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+        out[static_cast<uint64_t>(row) * head_dim + d] = *reinterpret_cast<uint16_t *>(&v);
+    }
+}
+
+// ---------------------------------------------------------------- host-side planning
+uint32_t target_ctas() { return 16u * static_cast<uint32_t>(sm_count()); }  // 8 waves x 2/SM
+
+uint32_t choose_chunk(uint32_t batch, uint32_t kv_heads, uint32_t range_len) {
+    const uint64_t rows = static_cast<uint64_t>(batch) * kv_heads * std::max<uint32_t>(range_len, 1);
+    uint64_t c = (rows + target_ctas() - 1) / target_ctas();
+    c = (c + kStagePos - 1) / kStagePos * kStagePos;
+    return static_cast<uint32_t>(std::min<uint64_t>(std::max<uint64_t>(c, kStagePos), 1u << 24));
+}
+
+uint32_t max_splits_for(uint32_t batch, uint32_t kv_heads, uint32_t max_len) {
+    const uint64_t by_len = (static_cast<uint64_t>(max_len) + kStagePos - 1) / kStagePos;
+    const uint64_t by_target = target_ctas() / std::max<uint64_t>(1, static_cast<uint64_t>(batch) * kv_heads) + 2;
+    return static_cast<uint32_t>(std::max<uint64_t>(1, std::min(by_len, by_target)));
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+size_t workspace_bytes(uint32_t batch, uint32_t q_heads, uint32_t kv_heads, uint32_t max_len) {
+    const size_t parts = static_cast<size_t>(batch) * q_heads * max_splits_for(batch, kv_heads, max_len) *
+                         kWsRec * sizeof(float);
+    return align256(parts) + align256(static_cast<size_t>(batch) * kv_heads * sizeof(unsigned));
+}
+
+int check_params(const apex_attn_params *p, const char *name) {
+    if (!p) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": null params");
+    if (p->head_dim != kD)
+        return fail(APEX_ERR_UNSUPPORTED, std::string(name) + ": this build supports head_dim 256");
+    if (p->kv_heads == 0 || p->q_heads != p->kv_heads * kG)
+        return fail(APEX_ERR_UNSUPPORTED, std::string(name) + ": this build supports q_heads = 2 * kv_heads");
+    if (p->rope_pairs > kD / 2)
+        return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": rope_pairs > head_dim / 2");
+    if (p->kv_heads > 65535) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": too many kv heads");
+    return APEX_OK;
+}
+
+int launch_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t *k_new,
+                  const uint16_t *v_new, const uint16_t *q_w, const uint16_t *k_w,
+                  uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
+                  const int32_t *seq_lens, uint32_t batch, uint32_t max_seq_len,
+                  uint32_t kv_begin, uint32_t kv_end, bool partial_mode, uint16_t *out,
+                  float *partial_out, void *workspace, size_t workspace_bytes_given, void *stream,
+                  const char *name) {
+    int rc = check_params(p, name);
+    if (rc) return rc;
+    if (batch == 0) return ok();
+    if (batch > 65535) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": batch > 65535");
+    if (!q_raw || !k_new || !v_new || !k_cache || !v_cache || !seq_lens ||
+        (partial_mode ? !partial_out : !out))
+        return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": null tensor");
+    for (const void *ptr : {(const void *)q_raw, (const void *)k_new, (const void *)v_new,
+                            (const void *)k_cache, (const void *)v_cache})
+        if (!aligned16(ptr)) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": tensors must be 16-byte aligned");
+    if (max_seq_len == 0) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": max_seq_len must be >= 1");
+    if (kv_end <= kv_begin) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": empty kv range");
+    const uint32_t range_len = std::min<uint32_t>(kv_end, max_seq_len) - std::min(kv_begin, max_seq_len);
+    if ((partial_mode ? static_cast<uint64_t>(kv_end) - kv_begin : max_seq_len) > capacity)
+        return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": key range exceeds cache capacity");
+    const size_t need = workspace_bytes(batch, p->q_heads, p->kv_heads, max_seq_len);
+    if (!workspace || workspace_bytes_given < need)
+        return fail(APEX_ERR_WORKSPACE, std::string(name) + ": workspace of " + std::to_string(need) +
+                                            " bytes required");
+    if (!aligned16(workspace)) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": workspace must be 16-byte aligned");
+
+    DecodeArgs a{};
+    a.q_raw = q_raw; a.k_new = k_new; a.v_new = v_new; a.q_w = q_w; a.k_w = k_w;
+    a.k_cache = k_cache; a.v_cache = v_cache; a.seq_lens = seq_lens;
+    a.out = out; a.partial_out = partial_out;
+    const uint32_t max_splits = max_splits_for(batch, p->kv_heads, max_seq_len);
+    a.ws_part = static_cast<float *>(workspace);
+    a.ws_count = reinterpret_cast<unsigned *>(
+        static_cast<uint8_t *>(workspace) +
+        align256(static_cast<size_t>(batch) * p->q_heads * max_splits * kWsRec * sizeof(float)));
+    a.capacity = capacity; a.q_heads = p->q_heads; a.kv_heads = p->kv_heads;
+    a.rope_pairs = p->rope_pairs; a.window = p->window; a.qk_norm = p->qk_norm; a.v_norm = p->v_norm;
+    a.chunk = choose_chunk(batch, p->kv_heads, range_len);
+    a.max_splits = max_splits;
+    a.kv_begin = kv_begin; a.kv_end = kv_end; a.max_seq_len = max_seq_len;
+    a.rope_base = p->rope_base; a.eps = p->eps; a.scale_log2 = p->scale * kLog2e;
+    a.partial_mode = partial_mode ? 1 : 0;
+    a.status = device_status_ptr();
+    if (!a.status) return fail(APEX_ERR_CUDA, std::string(name) + ": device status word unavailable");
+    const uint32_t grid_x = std::max<uint32_t>(1, (std::max<uint32_t>(range_len, 1) + a.chunk - 1) / a.chunk);
+    if (grid_x > max_splits)
+        return fail(APEX_ERR_WORKSPACE, std::string(name) + ": internal split plan exceeds workspace");
+
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+        rc = check_cuda(cudaFuncSetAttribute(decode_splitkv_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(sizeof(DecodeSmem))),
+                        "decode smem attribute");
+        if (rc) return rc;
+        attr_set[dev] = true;
+    }
+    const dim3 grid(grid_x, p->kv_heads, batch);
+    decode_splitkv_kernel<<<grid, kThreads, sizeof(DecodeSmem), static_cast<cudaStream_t>(stream)>>>(a);
+    rc = check_cuda(cudaGetLastError(), name);
+    return rc ? rc : ok();
+}
+
+}  // namespace
+}  // namespace apex
+
+extern "C" size_t apex_attn_decode_workspace_bytes(const apex_attn_params *p, uint32_t batch,
+                                                   uint32_t max_seq_len) {
+    if (!p || p->kv_heads == 0) return 0;
+    return apex::workspace_bytes(batch, p->q_heads, p->kv_heads, std::max<uint32_t>(max_seq_len, 1));
+}
+
+extern "C" int apex_attn_decode_workspace_init(void *workspace, size_t workspace_bytes,
+                                               void *stream) {
+    if (!workspace) return apex::fail(APEX_ERR_WORKSPACE, "apex_attn_decode_workspace_init: null workspace");
+    const int rc = apex::check_cuda(
+        cudaMemsetAsync(workspace, 0, workspace_bytes, static_cast<cudaStream_t>(stream)),
+        "apex_attn_decode_workspace_init");
+    return rc ? rc : apex::ok();
+}
+
+extern "C" int apex_attn_decode_bf16(const apex_attn_params *p, const uint16_t *q_raw,
+                                     const uint16_t *k_new, const uint16_t *v_new,
+                                     const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                                     uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
+                                     const int32_t *seq_lens, uint32_t batch,
+                                     uint32_t max_seq_len, uint16_t *out, void *workspace,
+                                     size_t workspace_bytes, void *stream) {
+    return apex::launch_decode(p, q_raw, k_new, v_new, q_norm_w, k_norm_w, k_cache, v_cache,
+                               capacity, seq_lens, batch, max_seq_len, 0, 0xffffffffu, false, out,
+                               nullptr, workspace, workspace_bytes, stream, "apex_attn_decode_bf16");
+}
+
+extern "C" int apex_attn_decode_partial_bf16(const apex_attn_params *p, const uint16_t *q_raw,
+                                             const uint16_t *k_new, const uint16_t *v_new,
+                                             const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                                             uint16_t *k_cache, uint16_t *v_cache,
+                                             uint32_t capacity, const int32_t *seq_lens,
+                                             uint32_t batch, uint32_t max_seq_len,
+                                             uint32_t kv_begin, uint32_t kv_end, float *partial,
+                                             void *workspace, size_t workspace_bytes,
+                                             void *stream) {
+    return apex::launch_decode(p, q_raw, k_new, v_new, q_norm_w, k_norm_w, k_cache, v_cache,
+                               capacity, seq_lens, batch, max_seq_len, kv_begin, kv_end, true,
+                               nullptr, partial, workspace, workspace_bytes, stream,
+                               "apex_attn_decode_partial_bf16");
+}
+
+extern "C" int apex_attn_merge_partials(const float *partials, uint32_t num_partials,
+                                        uint32_t rows, uint32_t head_dim, uint16_t *out,
+                                        void *stream) {
+    using namespace apex;
+    if (rows == 0) return ok();
+    if (!partials || !out) return fail(APEX_ERR_INVALID_ARGUMENT, "apex_attn_merge_partials: null tensor");
+    if (num_partials == 0 || head_dim == 0)
+        return fail(APEX_ERR_INVALID_ARGUMENT, "apex_attn_merge_partials: empty partial set");
+    merge_partials_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(partials, num_partials,
+                                                                              rows, head_dim, out);
+    const int rc = check_cuda(cudaGetLastError(), "apex_attn_merge_partials");
+    return rc ? rc : ok();
+}

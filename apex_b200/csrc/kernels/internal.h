@@ -1,0 +1,33 @@
+// internal.h -- host-side helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "../../../include/apex_cuda.h"
+
+namespace apex {
+
+// Records `msg` as this thread's last error and returns `code`.
+int fail(int code, const std::string &msg);
+// Checks a CUDA runtime result; on failure records it and returns APEX_ERR_CUDA.
+int check_cuda(cudaError_t e, const char *what);
+// Clears this thread's last error and returns APEX_OK.
+int ok();
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+// Device address of the current device's status word (see kStatusTimeout), or null.
+unsigned *device_status_ptr();
+
+// A 3-D bf16 tensor map with 128-byte swizzle: dims {d0 (innermost, elements), d1, d2},
+// byte strides of dims 1 and 2, box {box0, box1, 1}.  Out-of-range elements read as zero.
+int make_tensor_map_bf16_3d(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1,
+                            uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                            uint32_t box0, uint32_t box1);
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace apex

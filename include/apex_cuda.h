@@ -1,0 +1,195 @@
+/*
+ * apex_cuda.h -- C ABI of the B200 (sm_100a) attention hot path.
+ *
+ * The drop-in boundary for the reference's attention stage: per-head QK RMSNorm + RoPE fused
+ * into grouped-query attention over a KV cache.  Plain pointers and sizes only.  Every
+ * pointer argument named as a tensor is a DEVICE pointer unless stated otherwise; `stream`
+ * is a cudaStream_t passed as void* (NULL = legacy default stream).  Calls only enqueue work;
+ * they return before the GPU finishes, like the reference's Backend::run
+ * (src/backend/backend.h:55-56), and report launch-time errors as a nonzero status.
+ *
+ * Reference interfaces replaced (paths inside the spotta85/apex tree):
+ *   apex_head_norm_rope_f32   kernel head_norm_rope_f32 (shaders/head_norm_rope.metal:5-20),
+ *                             launched by apex::headNormRope (src/ops.h:88-122) through
+ *                             Backend::run (src/backend/backend.h:55-56)
+ *   apex_attention_f32        kernel attention_f32 (docs/B6_3_attention.md:282-295), launched
+ *                             by apex::attention (docs/B6_3_attention.md:424-431)
+ *   apex_head_norm_rope_bf16, apex_attn_decode_bf16, apex_attn_decode_partial_bf16,
+ *   apex_attn_merge_partials, apex_attn_prefill_bf16
+ *                             the bf16 KV-cache path the reference plans (f16 cache,
+ *                             docs/B6_3_attention.md:99-102) with the steps of
+ *                             apex::attentionBlock between its projections
+ *                             (docs/B6_3_attention.md:444-454) fused per call.
+ */
+#ifndef APEX_CUDA_H
+#define APEX_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define APEX_API __attribute__((visibility("default")))
+#else
+#define APEX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define APEX_OK 0
+#define APEX_ERR_INVALID_ARGUMENT 1 /* a size, pointer, alignment or stride was rejected */
+#define APEX_ERR_UNSUPPORTED 2      /* valid request this build has no kernel for */
+#define APEX_ERR_CUDA 3             /* a CUDA runtime call failed */
+#define APEX_ERR_WORKSPACE 4        /* workspace missing or too small */
+#define APEX_ERR_DEVICE_TIMEOUT 5   /* a kernel's bounded wait gave up (see apex_cuda_device_status) */
+
+/* Attention geometry and numerics of one layer: the reference's AttentionShape
+ * (docs/B6_3_attention.md:365-372) plus the knobs the bf16 configurations need.
+ *   scale    softmax scale (the reference model uses 1.0, docs/B6_3_attention.md:27)
+ *   qk_norm  1: RMSNorm q and k over head_dim (weights optional), 0: no norm
+ *   v_norm   1: weightless RMSNorm of v (the reference model, docs/B6_3_attention.md:25)
+ *   window   0 = global causal; else key j is visible to the query at position p iff
+ *            p - window < j <= p (docs/B6_3_attention.md:42)                              */
+typedef struct apex_attn_params {
+    uint32_t q_heads;
+    uint32_t kv_heads;
+    uint32_t head_dim;
+    uint32_t rope_pairs; /* pairs (i, i + head_dim/2) rotated, 0 = no RoPE */
+    float rope_base;
+    uint32_t window;
+    float scale;
+    float eps;
+    uint32_t qk_norm;
+    uint32_t v_norm;
+} apex_attn_params;
+
+/* Message of the last failing call on this host thread ("" if none). */
+APEX_API const char *apex_cuda_last_error(void);
+/* ABI version of this library (major * 100 + minor). */
+APEX_API int apex_cuda_abi_version(void);
+/* Reads and clears the device-side status word written by kernels whose bounded waits gave
+ * up; synchronises `stream`.  Returns APEX_OK or APEX_ERR_DEVICE_TIMEOUT. */
+APEX_API int apex_cuda_device_status(void *stream);
+
+/* ------------------------------------------------------------------ f32 drop-ins */
+
+/* Per (token, head): RMSNorm over head_dim with an optional bf16 weight, then RoPE on the
+ * first rope_pairs pairs (i, i + head_dim/2) at position abs_pos + token, written to
+ * output[token * out_token_stride + head * out_head_stride + d].  input is
+ * [tokens][heads][head_dim] f32; weight is head_dim raw bf16 bits (read iff has_weight).
+ * input == output is allowed when the strides equal the input layout.  head_dim <= 512,
+ * even.  Same arguments, in the same order, as src/ops.h:88-122. */
+APEX_API int apex_head_norm_rope_f32(const float *input, const uint16_t *weight, float *output,
+                            uint32_t tokens, uint32_t heads, uint32_t head_dim,
+                            uint32_t has_weight, uint32_t rope_pairs, float rope_base,
+                            uint32_t abs_pos, uint32_t out_token_stride,
+                            uint32_t out_head_stride, float eps, void *stream);
+
+/* Softmax over keys for every (token, q head), scale 1.0, as attention_f32.
+ * q, out [tokens][q_heads][head_dim]; K, V [kv_heads][capacity][head_dim] f32; the query of
+ * token t sits at position pos0 + t and sees keys per `window`.  head_dim <= 512. */
+APEX_API int apex_attention_f32(const float *q, const float *K, const float *V, float *out,
+                       uint32_t tokens, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                       uint32_t capacity, uint32_t pos0, uint32_t window, void *stream);
+
+/* apex_attention_f32 with an explicit softmax scale. */
+APEX_API int apex_attention_f32_scaled(const float *q, const float *K, const float *V, float *out,
+                              uint32_t tokens, uint32_t q_heads, uint32_t kv_heads,
+                              uint32_t head_dim, uint32_t capacity, uint32_t pos0,
+                              uint32_t window, float scale, void *stream);
+
+/* ------------------------------------------------------------------ bf16 hot path */
+
+/* apex_head_norm_rope_f32 on bf16 input/output (the K/V cache append of the bf16 path).
+ * All bf16 tensors are raw uint16 bits. */
+APEX_API int apex_head_norm_rope_bf16(const uint16_t *input, const uint16_t *weight, uint16_t *output,
+                             uint32_t tokens, uint32_t heads, uint32_t head_dim,
+                             uint32_t has_weight, uint32_t rope_pairs, float rope_base,
+                             uint32_t abs_pos, uint32_t out_token_stride,
+                             uint32_t out_head_stride, float eps, void *stream);
+
+/* Workspace bytes apex_attn_decode_bf16 needs for up to `batch` sequences of at most
+ * max_seq_len keys (split-KV partials + per-(sequence, kv head) counters). */
+APEX_API size_t apex_attn_decode_workspace_bytes(const apex_attn_params *p, uint32_t batch,
+                                        uint32_t max_seq_len);
+/* Zero the workspace's counters; required once before the first decode call that uses it
+ * (every call leaves them zero again). */
+APEX_API int apex_attn_decode_workspace_init(void *workspace, size_t workspace_bytes, void *stream);
+
+/* One decode step of `batch` sequences, fused: for each sequence b with seq_lens[b] keys
+ * (the new token included, at position seq_lens[b]-1):
+ *   q    = rope(rmsnorm(q_raw[b], q_norm_w))                      -- in registers
+ *   K[b][:, L-1] = rope(rmsnorm(k_new[b], k_norm_w)), V[b][:, L-1] = [rmsnorm](v_new[b])
+ *   out[b] = softmax(scale * q K^T) V over the visible keys          (split-KV, LSE merge)
+ * q_raw [B][Hq][D]; k_new, v_new [B][Hkv][D]; caches [B][Hkv][capacity][D]; seq_lens is a
+ * DEVICE int32 [B] with 1 <= seq_lens[b] <= max_seq_len <= capacity; out [B][Hq][D].
+ * Norm weights are bf16 [D] or NULL (weight 1.0).  head_dim 256, Hq / Hkv = 2. */
+APEX_API int apex_attn_decode_bf16(const apex_attn_params *p, const uint16_t *q_raw,
+                          const uint16_t *k_new, const uint16_t *v_new,
+                          const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                          uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
+                          const int32_t *seq_lens, uint32_t batch, uint32_t max_seq_len,
+                          uint16_t *out, void *workspace, size_t workspace_bytes,
+                          void *stream);
+
+/* KV-sequence-split decode: this caller holds global key positions [kv_begin, kv_end) of
+ * every sequence, stored at local cache index (position - kv_begin).  Same fused step as
+ * apex_attn_decode_bf16 restricted to those keys (the new token is appended here only if
+ * seq_lens[b]-1 falls in the range), producing one partial per (b, q head):
+ *   partial[(b*Hq + h)*(D+2) + d] = o_d (normalised),  [.. + D] = m (log2 units),
+ *   [.. + D+1] = l, with m = max_j s_j*scale*log2(e), l = sum_j 2^(s_j*scale*log2e - m).
+ * A sequence with no keys in the range gets l = 0.  max_seq_len bounds the GLOBAL length. */
+APEX_API int apex_attn_decode_partial_bf16(const apex_attn_params *p, const uint16_t *q_raw,
+                                  const uint16_t *k_new, const uint16_t *v_new,
+                                  const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                                  uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
+                                  const int32_t *seq_lens, uint32_t batch,
+                                  uint32_t max_seq_len, uint32_t kv_begin, uint32_t kv_end,
+                                  float *partial, void *workspace, size_t workspace_bytes,
+                                  void *stream);
+
+/* Log-sum-exp merge of num_partials partial sets laid out [num_partials][rows][D+2] (the
+ * apex_attn_decode_partial_bf16 format, e.g. after an all-gather) into out [rows][D] bf16. */
+APEX_API int apex_attn_merge_partials(const float *partials, uint32_t num_partials, uint32_t rows,
+                             uint32_t head_dim, uint16_t *out, void *stream);
+
+/* Workspace bytes apex_attn_prefill_bf16 needs (the normalised, head-major Q). */
+APEX_API size_t apex_attn_prefill_workspace_bytes(const apex_attn_params *p, uint32_t batch,
+                                         uint32_t tokens);
+
+/* The first stage of apex_attn_prefill_bf16 on its own: q/k norm + RoPE, K/V appended to the
+ * caches at pos0, normalised q written head-major to q_normed [B][Hq][T][D] (bf16). */
+APEX_API int apex_attn_prefill_prep_bf16(const apex_attn_params *p, const uint16_t *q_raw,
+                                         const uint16_t *k_raw, const uint16_t *v_raw,
+                                         const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                                         uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
+                                         uint32_t batch, uint32_t tokens, uint32_t pos0,
+                                         uint16_t *q_normed, void *stream);
+
+/* The second stage on its own: tcgen05 attention of q_normed [B][Hq][T][D] (queries at pos0..)
+ * over cache positions [0, pos0+tokens) -> out [B][T][Hq][D]. */
+APEX_API int apex_attn_prefill_attend_bf16(const apex_attn_params *p, const uint16_t *q_normed,
+                                           const uint16_t *k_cache, const uint16_t *v_cache,
+                                           uint32_t capacity, uint32_t batch, uint32_t tokens,
+                                           uint32_t pos0, uint16_t *out, void *stream);
+
+/* Causal (optionally sliding-window) prefill of `tokens` new tokens per sequence at
+ * positions pos0 .. pos0+tokens-1, fused: q/k norm + RoPE, K/V appended to the caches, then
+ * attention over cache positions [0, pos0+tokens) on tcgen05 tensor cores.
+ * q_raw [B][T][Hq][D]; k_raw, v_raw [B][T][Hkv][D]; caches [B][Hkv][capacity][D] with
+ * positions < pos0 already filled; out [B][T][Hq][D].  head_dim 256; 16-byte aligned
+ * pointers. */
+APEX_API int apex_attn_prefill_bf16(const apex_attn_params *p, const uint16_t *q_raw,
+                           const uint16_t *k_raw, const uint16_t *v_raw,
+                           const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                           uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
+                           uint32_t batch, uint32_t tokens, uint32_t pos0, uint16_t *out,
+                           void *workspace, size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* APEX_CUDA_H */
