@@ -32,7 +32,7 @@ NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompil
 
 KERNEL_SOURCES = sorted((CSRC / "kernels").glob("*.cu"))
 BACKEND_SOURCES = sorted((CSRC / "backend" / "cuda").glob("*.cpp"))
-CLI_SOURCES = sorted((CSRC / "tests").glob("*.cpp")) + [CSRC / "main.cpp"]
+CLI_SOURCES = [CSRC / "main.cpp"]
 
 
 def nvcc() -> str:
@@ -78,8 +78,7 @@ def build(verbose: bool = False, force: bool = False) -> pathlib.Path:
     cli_srcs = [s for s in CLI_SOURCES if s.exists()]
     if cli_srcs and (force or _stale(CLI, cli_srcs + headers + [LIB])):
         _run([nvcc(), *ARCH, *NVCC_FLAGS, "-x", "cu", *map(str, cli_srcs), "-o", str(CLI),
-              "-L", str(LIB_DIR), "-lapex_cuda", "-Xlinker", "-rpath=$ORIGIN",
-              "-I", str(ROOT / "oracle")], verbose)
+              "-L", str(LIB_DIR), "-lapex_cuda", "-Xlinker", "-rpath=$ORIGIN"], verbose)
     return LIB
 
 
