@@ -26,7 +26,7 @@ EXPORTED = (
     "apex_head_norm_rope_bf16", "apex_attn_decode_workspace_bytes",
     "apex_attn_decode_workspace_init", "apex_attn_decode_bf16", "apex_attn_decode_partial_bf16",
     "apex_attn_merge_partials", "apex_attn_prefill_workspace_bytes", "apex_attn_prefill_bf16",
-    "apex_attn_prefill_prep_bf16", "apex_attn_prefill_attend_bf16",
+    "apex_attn_prefill_prep_bf16", "apex_attn_prefill_attend_bf16", "apex_attn_decode_bf16_noalloc",
 )
 
 
@@ -70,6 +70,7 @@ def load(path: str | pathlib.Path | None = None):
     L.apex_attn_decode_workspace_bytes.restype = _sz
     L.apex_attn_decode_workspace_init.argtypes = [_vp, _sz, _vp]
     L.apex_attn_decode_bf16.argtypes = ([_PP] + [_vp] * 7 + [_u32, _vp, _u32, _u32, _vp, _vp, _sz, _vp])
+    L.apex_attn_decode_bf16_noalloc.argtypes = ([_PP] + [_vp] * 7 + [_u32, _vp, _u32, _u32, _vp, _vp])
     L.apex_attn_decode_partial_bf16.argtypes = ([_PP] + [_vp] * 7 + [_u32, _vp, _u32, _u32, _u32, _u32,
                                                                        _vp, _vp, _sz, _vp])
     L.apex_attn_merge_partials.argtypes = [_vp, _u32, _u32, _u32, _vp, _vp]

@@ -21,6 +21,8 @@
 // single ex2 instructions.  Warps merge once per CTA; the last CTA of each (b, kv head)
 // (atomic counter, no spin) merges the split partials and writes bf16 -- one launch per step.
 #include <algorithm>
+#include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "internal.h"
@@ -592,4 +594,78 @@ extern "C" int apex_attn_merge_partials(const float *partials, uint32_t num_part
                                                                               rows, head_dim, out);
     const int rc = check_cuda(cudaGetLastError(), "apex_attn_merge_partials");
     return rc ? rc : ok();
+}
+
+// ---------------------------------------------------------------- allocation-free variant
+// Some callers cannot call cudaMalloc for the decode workspace: an engine that owns all of
+// its device memory under a fixed budget (the design of the engine this path comes from) has
+// nowhere to put a library allocation, and a latency-critical decode loop cannot pay for
+// cudaMalloc's implicit device synchronisation.  apex_attn_decode_bf16_noalloc serves them
+// from this file-scope device array instead.  It is a fixed 8 MiB: every GPU the library is
+// used on holds it until the process exits.  The decode kernel receives its address; host
+// code only names it to look that address up.
+namespace apex {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) uint8_t g_decode_scratch[kNoAllocScratchBytes];
+
+// Device address of g_decode_scratch on the current device, looked up once per device (the
+// symbol's host-side name is only a stand-in, never a device address).
+int noalloc_scratch(void **ptr) {
+    static std::mutex mu;
+    static std::vector<void *> cache;
+    int dev = 0;
+    int rc = check_cuda(cudaGetDevice(&dev), "apex_attn_decode_bf16_noalloc: cudaGetDevice");
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(mu);
+    if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1, nullptr);
+    if (!cache[dev]) {
+        void *p = nullptr;
+        rc = check_cuda(cudaGetSymbolAddress(&p, g_decode_scratch),
+                        "apex_attn_decode_bf16_noalloc: cudaGetSymbolAddress");
+        if (rc) return rc;
+        cache[dev] = p;
+    }
+    *ptr = cache[dev];
+    return APEX_OK;
+}
+
+}  // namespace
+}  // namespace apex
+
+extern "C" int apex_attn_decode_bf16_noalloc(const apex_attn_params *p, const uint16_t *q_raw,
+                                             const uint16_t *k_new, const uint16_t *v_new,
+                                             const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                                             uint16_t *k_cache, uint16_t *v_cache,
+                                             uint32_t capacity, const int32_t *seq_lens,
+                                             uint32_t batch, uint32_t max_seq_len, uint16_t *out,
+                                             void *stream) {
+    using namespace apex;
+    const char *name = "apex_attn_decode_bf16_noalloc";
+    int rc = check_params(p, name);
+    if (rc) return rc;
+    if (batch == 0) return ok();
+    const uint32_t msl = std::max<uint32_t>(max_seq_len, 1);
+    const size_t need = workspace_bytes(batch, p->q_heads, p->kv_heads, msl);
+    if (need > kNoAllocScratchBytes)
+        return fail(APEX_ERR_WORKSPACE,
+                    std::string(name) + ": batch " + std::to_string(batch) + " x max_seq_len " +
+                        std::to_string(msl) + " needs " + std::to_string(need) +
+                        " bytes of scratch; the static scratch holds " +
+                        std::to_string(kNoAllocScratchBytes) + " (use apex_attn_decode_bf16)");
+    void *scratch = nullptr;
+    rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    // The split counters must start at zero; the array keeps whatever the last call left.
+    const size_t counters_off = align256(static_cast<size_t>(batch) * p->q_heads *
+                                         max_splits_for(batch, p->kv_heads, msl) * kWsRec * sizeof(float));
+    rc = check_cuda(cudaMemsetAsync(static_cast<uint8_t *>(scratch) + counters_off, 0,
+                                    static_cast<size_t>(batch) * p->kv_heads * sizeof(unsigned),
+                                    static_cast<cudaStream_t>(stream)),
+                    "apex_attn_decode_bf16_noalloc: clear counters");
+    if (rc) return rc;
+    return launch_decode(p, q_raw, k_new, v_new, q_norm_w, k_norm_w, k_cache, v_cache, capacity, seq_lens,
+                         batch, max_seq_len, 0, 0xffffffffu, false, out, nullptr, scratch,
+                         kNoAllocScratchBytes, stream, name);
 }

@@ -134,6 +134,27 @@ APEX_API int apex_attn_decode_bf16(const apex_attn_params *p, const uint16_t *q_
                           uint16_t *out, void *workspace, size_t workspace_bytes,
                           void *stream);
 
+/* apex_attn_decode_bf16 for callers that cannot allocate device memory: an engine that keeps
+ * all of its device memory under its own fixed budget, or a decode loop that cannot take
+ * cudaMalloc's implicit synchronisation.  Same arguments minus the workspace.  It has no
+ * counterpart in the reference.
+ *   - Scratch is a static 8 MiB device array inside this library, reserved on every GPU the
+ *     library is used on until the process exits.  Requests that need more (the size
+ *     apex_attn_decode_workspace_bytes reports for batch x max_seq_len; all five benchmark
+ *     configurations fit) fail with APEX_ERR_WORKSPACE and launch nothing.
+ *   - The first call on each device looks up the array's device address (once per device);
+ *     make that first call before any stream capture.
+ *   - Allocates nothing: no cudaMalloc, no cudaFree, no allocating library routine.  Each
+ *     call clears the scratch counters it needs on `stream` before the kernel.
+ *   - Every call shares the one array: calls whose execution overlaps on the GPU (other
+ *     streams, other host threads) race and corrupt each other's results; serialise them. */
+APEX_API int apex_attn_decode_bf16_noalloc(const apex_attn_params *p, const uint16_t *q_raw,
+                                           const uint16_t *k_new, const uint16_t *v_new,
+                                           const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                                           uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
+                                           const int32_t *seq_lens, uint32_t batch,
+                                           uint32_t max_seq_len, uint16_t *out, void *stream);
+
 /* KV-sequence-split decode: this caller holds global key positions [kv_begin, kv_end) of
  * every sequence, stored at local cache index (position - kv_begin).  Same fused step as
  * apex_attn_decode_bf16 restricted to those keys (the new token is appended here only if
