@@ -77,8 +77,8 @@ def load(path: str | pathlib.Path | None = None):
     L.apex_attn_prefill_workspace_bytes.argtypes = [_PP, _u32, _u32]
     L.apex_attn_prefill_workspace_bytes.restype = _sz
     L.apex_attn_prefill_bf16.argtypes = ([_PP] + [_vp] * 7 + [_u32, _u32, _u32, _u32, _vp, _vp, _sz, _vp])
-    L.apex_attn_prefill_prep_bf16.argtypes = ([_PP] + [_vp] * 7 + [_u32, _u32, _u32, _u32, _vp, _vp])
-    L.apex_attn_prefill_attend_bf16.argtypes = ([_PP] + [_vp] * 3 + [_u32, _u32, _u32, _u32, _vp, _vp])
+    L.apex_attn_prefill_prep_bf16.argtypes = ([_PP] + [_vp] * 7 + [_u32, _u32, _u32, _u32, _vp, _sz, _vp])
+    L.apex_attn_prefill_attend_bf16.argtypes = ([_PP, _vp, _sz, _vp, _vp] + [_u32, _u32, _u32, _u32, _vp, _vp])
     for fn in EXPORTED:
         if fn not in ("apex_cuda_last_error", "apex_attn_decode_workspace_bytes",
                       "apex_attn_prefill_workspace_bytes"):

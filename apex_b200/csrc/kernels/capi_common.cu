@@ -1,5 +1,6 @@
 // capi_common.cu -- error reporting, device status word, SM count and tensor-map encoding
 // shared by every C-ABI entry point.
+#include <cmath>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -64,6 +65,13 @@ int sm_count() {
         cache[dev] = n > 0 ? n : 148;
     }
     return cache[dev];
+}
+
+void rope_table(float *inv_freq, uint32_t pairs, uint32_t head_dim, float base) {
+    for (uint32_t i = 0; i < pairs; ++i) {
+        const float e = -2.0f * static_cast<float>(i) / static_cast<float>(head_dim);
+        inv_freq[i] = static_cast<float>(std::pow(static_cast<double>(base), static_cast<double>(e)));
+    }
 }
 
 unsigned *device_status_ptr() {

@@ -27,11 +27,21 @@ __device__ __forceinline__ float bf16_round(float x) {
     return __bfloat162float(__float2bfloat16_rn(x));
 }
 
-// RoPE inverse frequency base^(-2i/hd), rounded once to f32 from a double-precision pow (the
-// reference evaluates pow(base, -2i/hd) in f32 with a correctly rounded library pow).
-__device__ __forceinline__ float rope_inv_freq(uint32_t i, uint32_t head_dim, float base) {
-    const float e = -2.0f * (float)i / (float)head_dim;
-    return (float)pow((double)base, (double)e);
+// RoPE inverse frequencies inv_freq[i] = base^(-2i/hd) for i < pairs, computed once on the host
+// (rope_table) and passed by value; kernels stage the table in shared memory.
+constexpr int kMaxRopePairs = 256;
+struct RopeTable {
+    float inv_freq[kMaxRopePairs];
+};
+
+// cos and sin of an f32 angle, reduced in double precision (the angle itself is the f32 product
+// pos * inv_freq, as the reference computes it); avoids the f32 slow path for the large angles
+// of long contexts.
+__device__ __forceinline__ void sincos_angle(float angle, float &s, float &c) {
+    double ds, dc;
+    sincos(static_cast<double>(angle), &ds, &dc);
+    s = static_cast<float>(ds);
+    c = static_cast<float>(dc);
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -138,6 +148,16 @@ __device__ __forceinline__ void tc_mma_ss(uint32_t d_tmem, uint64_t a_desc, uint
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16; A is M x 16 bf16 in TMEM (lane = row, two
+// elements per 32-bit column, 8 columns per MMA), K-major.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 // Arrive once on `bar` when all previously issued tcgen05.mma of this thread complete.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {

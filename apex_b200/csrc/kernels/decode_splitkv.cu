@@ -57,6 +57,7 @@ struct DecodeArgs {
     uint32_t chunk, max_splits, kv_begin, kv_end, max_seq_len;
     float rope_base, eps, scale_log2;
     int partial_mode;
+    RopeTable rope;      // inv_freq[i] = rope_base^(-2i/256)
 };
 
 struct __align__(16) DecodeSmem {
@@ -67,6 +68,7 @@ struct __align__(16) DecodeSmem {
     uint16_t new_v[kD];
     float inv_freq[kD / 2];
     float wm[kConsumerWarps][kG], wl[kConsumerWarps][kG];
+    float red[kConsumerWarps][kG];
     uint64_t full[kStages], empty[kStages];
     int is_last;
 };
@@ -163,7 +165,32 @@ __device__ __forceinline__ void warp_step(const uint8_t *kbase, const uint8_t *v
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const DecodeArgs a) {
+// Max (or sum) over the 128 consumer threads of one value per head, using red[][] in shared
+// memory; every consumer thread gets the result.
+template <bool kMax>
+__device__ __forceinline__ void consumer_reduce(float (&v)[kG], float (&red)[kConsumerWarps][kG], uint32_t warp,
+                                                uint32_t lane) {
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float t = __shfl_xor_sync(0xffffffffu, v[g], o);
+            v[g] = kMax ? fmaxf(v[g], t) : v[g] + t;
+        }
+        if (lane == 0) red[warp][g] = v[g];
+    }
+    consumer_sync();
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+        float r = red[0][g];
+#pragma unroll
+        for (int w = 1; w < kConsumerWarps; ++w) r = kMax ? fmaxf(r, red[w][g]) : r + red[w][g];
+        v[g] = r;
+    }
+    consumer_sync();
+}
+
+__global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __grid_constant__ DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     DecodeSmem &sm = *reinterpret_cast<DecodeSmem *>(smem_raw);
 
@@ -230,8 +257,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const Decod
     }
 
     // -------------------------------------------------------------------- consumers
-    for (uint32_t i = tid; i < a.rope_pairs; i += kConsumerWarps * 32)
-        sm.inv_freq[i] = rope_inv_freq(i, kD, a.rope_base);
+    for (uint32_t i = tid; i < a.rope_pairs; i += kConsumerWarps * 32) sm.inv_freq[i] = a.rope.inv_freq[i];
     consumer_sync();
     const float pos_f = static_cast<float>(pos_new);
     if (warp < kG) {
@@ -373,26 +399,62 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const Decod
     consumer_sync();
     if (!sm.is_last) return;
     __threadfence();
-    const float *parts = a.ws_part + row * a.max_splits * kWsRec;
-    float Mx = -INFINITY;
-    for (uint32_t s = 0; s < nsplit; ++s) {
-        const float l_s = __ldcg(parts + s * kWsRec + kD + 1);
-        if (l_s > 0.f) Mx = fmaxf(Mx, __ldcg(parts + s * kWsRec + kD));
+    // Parallel log-sum-exp merge of the nsplit partials of both heads: per-split (m, l) staged in
+    // shared memory (the stage buffers are free), block reductions for the max and the sum,
+    // then each thread accumulates its 4 dims over the splits with independent 16-byte loads.
+    const float *parts0 = a.ws_part + (static_cast<uint64_t>(b) * Hq + kvh * kG) * a.max_splits * kWsRec;
+    float *ms = reinterpret_cast<float *>(sm.v[0]);  // [G][nsplit] m, then the weights
+    float *ls = ms + kG * nsplit;                      // [G][nsplit] l
+    float mx[kG] = {-INFINITY, -INFINITY};
+    for (uint32_t s = tid; s < nsplit; s += kConsumerWarps * 32) {
+#pragma unroll
+        for (int gg = 0; gg < kG; ++gg) {
+            const float *p = parts0 + (static_cast<uint64_t>(gg) * a.max_splits + s) * kWsRec;
+            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(p + kD));
+            ms[gg * nsplit + s] = ml.x;
+            ls[gg * nsplit + s] = ml.y;
+            if (ml.y > 0.f) mx[gg] = fmaxf(mx[gg], ml.x);
+        }
     }
-    float dsum = 0.f, r[4] = {0.f, 0.f, 0.f, 0.f};
-    for (uint32_t s = 0; s < nsplit; ++s) {
-        const float *p = parts + s * kWsRec;
-        const float l_s = __ldcg(p + kD + 1);
-        if (!(l_s > 0.f)) continue;
-        const float wt = fast_exp2(__ldcg(p + kD) - Mx) * l_s;
-        dsum += wt;
-        const float4 ov = __ldcg(reinterpret_cast<const float4 *>(p + d0));
+    consumer_reduce<true>(mx, sm.red, warp, lane);
+    float dsum[kG] = {0.f, 0.f};
+    for (uint32_t s = tid; s < nsplit; s += kConsumerWarps * 32) {
+#pragma unroll
+        for (int gg = 0; gg < kG; ++gg) {
+            const float l_s = ls[gg * nsplit + s];
+            const float wt = l_s > 0.f ? fast_exp2(ms[gg * nsplit + s] - mx[gg]) * l_s : 0.f;
+            ms[gg * nsplit + s] = wt;
+            dsum[gg] += wt;
+        }
+    }
+    consumer_reduce<false>(dsum, sm.red, warp, lane);  // its barriers also publish the weights
+    const float *pg = parts0 + static_cast<uint64_t>(g) * a.max_splits * kWsRec + d0;
+    const float *wg = ms + g * nsplit;
+    float r[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t s = 0;
+    for (; s + 4 <= nsplit; s += 4) {
+        float4 ov[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) ov[u] = __ldcg(reinterpret_cast<const float4 *>(pg + (s + u) * kWsRec));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float wt = wg[s + u];
+            r[0] += wt * ov[u].x;
+            r[1] += wt * ov[u].y;
+            r[2] += wt * ov[u].z;
+            r[3] += wt * ov[u].w;
+        }
+    }
+    for (; s < nsplit; ++s) {
+        const float4 ov = __ldcg(reinterpret_cast<const float4 *>(pg + s * kWsRec));
+        const float wt = wg[s];
         r[0] += wt * ov.x;
         r[1] += wt * ov.y;
         r[2] += wt * ov.z;
         r[3] += wt * ov.w;
     }
-    const float inv = dsum > 0.f ? 1.0f / dsum : 0.f;
+    const float Mx = mx[g], dtot = dsum[g];
+    const float inv = dtot > 0.f ? 1.0f / dtot : 0.f;
     if (a.partial_mode) {
         // A rank partial stores l relative to its own max Mx: l_rank = sum_s 2^(m_s - Mx) l_s.
         float *dst = a.partial_out + row * kPart;
@@ -400,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const Decod
         for (int e = 0; e < 4; ++e) dst[d0 + e] = r[e] * inv;
         if (d0 == 0) {
             dst[kD] = Mx;
-            dst[kD + 1] = dsum;
+            dst[kD + 1] = dtot;
         }
     } else {
         uint2 packed;
@@ -447,7 +509,8 @@ uint32_t choose_chunk(uint32_t batch, uint32_t kv_heads, uint32_t range_len) {
 uint32_t max_splits_for(uint32_t batch, uint32_t kv_heads, uint32_t max_len) {
     const uint64_t by_len = (static_cast<uint64_t>(max_len) + kStagePos - 1) / kStagePos;
     const uint64_t by_target = target_ctas() / std::max<uint64_t>(1, static_cast<uint64_t>(batch) * kv_heads) + 2;
-    return static_cast<uint32_t>(std::max<uint64_t>(1, std::min(by_len, by_target)));
+    // the last-CTA merge stages 2 * G * splits floats in the 48 KB of V stage buffers
+    return static_cast<uint32_t>(std::max<uint64_t>(1, std::min({by_len, by_target, uint64_t(3072)})));
 }
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -514,6 +577,7 @@ int launch_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16
     a.kv_begin = kv_begin; a.kv_end = kv_end; a.max_seq_len = max_seq_len;
     a.rope_base = p->rope_base; a.eps = p->eps; a.scale_log2 = p->scale * kLog2e;
     a.partial_mode = partial_mode ? 1 : 0;
+    rope_table(a.rope.inv_freq, p->rope_pairs, kD, p->rope_base);
     a.status = device_status_ptr();
     if (!a.status) return fail(APEX_ERR_CUDA, std::string(name) + ": device status word unavailable");
     const uint32_t grid_x = std::max<uint32_t>(1, (std::max<uint32_t>(range_len, 1) + a.chunk - 1) / a.chunk);

@@ -40,11 +40,10 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
                           T *output, uint32_t tokens, uint32_t heads, uint32_t head_dim,
                           uint32_t has_weight, uint32_t rope_pairs, float rope_base,
                           uint32_t abs_pos, uint32_t out_token_stride, uint32_t out_head_stride,
-                          float eps) {
+                          float eps, const __grid_constant__ RopeTable rope) {
     __shared__ float inv_freq[kMaxHeadDim / 2];
     __shared__ float rows[kRowsPerBlock][kMaxHeadDim];
-    for (uint32_t i = threadIdx.x; i < rope_pairs; i += blockDim.x)
-        inv_freq[i] = rope_inv_freq(i, head_dim, rope_base);
+    for (uint32_t i = threadIdx.x; i < rope_pairs; i += blockDim.x) inv_freq[i] = rope.inv_freq[i];
     __syncthreads();
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -73,7 +72,7 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
         const float pos = static_cast<float>(abs_pos + token);
         for (uint32_t i = lane; i < rope_pairs; i += 32) {
             float s, c;
-            sincosf(pos * inv_freq[i], &s, &c);
+            sincos_angle(pos * inv_freq[i], s, c);
             const float a = row[i], b = row[half + i];
             row[i] = a * c - b * s;
             row[half + i] = a * s + b * c;
@@ -101,9 +100,11 @@ int launch(const T *input, const uint16_t *weight, T *output, uint32_t tokens, u
     const uint64_t rows = static_cast<uint64_t>(tokens) * heads;
     const uint64_t want = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
     const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>(want, 16ull * sm_count()));
+    RopeTable rope{};
+    rope_table(rope.inv_freq, rope_pairs, head_dim, rope_base);
     head_norm_rope_kernel<T><<<grid, kRowsPerBlock * 32, 0, static_cast<cudaStream_t>(stream)>>>(
         input, weight, output, tokens, heads, head_dim, has_weight, rope_pairs, rope_base, abs_pos,
-        out_token_stride, out_head_stride, eps);
+        out_token_stride, out_head_stride, eps, rope);
     const int rc = check_cuda(cudaGetLastError(), name);
     return rc ? rc : ok();
 }

@@ -28,6 +28,10 @@ int make_tensor_map_bf16_3d(CUtensorMap *map, const void *base, uint64_t d0, uin
                             uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
                             uint32_t box0, uint32_t box1);
 
+// inv_freq[i] = base^(-2i/head_dim) (f32 exponent, double-precision power rounded to f32) for
+// i < pairs, the frequencies of shaders/head_norm_rope.metal:59.
+void rope_table(float *inv_freq, uint32_t pairs, uint32_t head_dim, float base);
+
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace apex

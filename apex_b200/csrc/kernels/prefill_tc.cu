@@ -7,24 +7,28 @@
 // o = softmax(scale * q K^T) V over keys p - window < j <= p (or j <= p), GQA map h/(Hq/Hkv).
 //
 // Two launches per call:
-//  1. prep: one warp per 256-wide row, 16-byte loads; q -> a head-major workspace
-//     [B][Hq][T][256] so a 128-query tile is one 3-D TMA box; k, v -> the caches.
-//  2. attention: one CTA per (128-query tile, q head), 8 warps:
-//       warp 0  TMA producer: Q tile once (64 KB), then K and V as 64-key half tiles (32 KB)
-//               through a 4-slot ring; 3-D tensor maps bound keys at pos0+T so keys past the
-//               cache end read as zeros (never uninitialised memory).
-//       warp 1  tcgen05.mma issuer (one thread) and TMEM owner (512 columns):
-//               S_j = Q K_j^T  (M=128, N=64 x 2, K=16 x 16, bf16 -> f32) into S[j%2],
-//               O  += P_j V_j  (M=128, N=256, K=16 x 8; V is the MN-major B operand).
-//               S_{j+1} is issued before PV_j, so the tensor pipe computes the next scores
-//               while the softmax warps work on the current ones.
-//       warps 4-7  softmax and epilogue, one query row per thread (TMEM lane = row):
-//               tcgen05.ld of the S row, causal/window mask only on boundary tiles, online
+//  1. prep: one warp per (sequence, token): the token's RoPE cos/sin are computed once and
+//     reused for its Hq + Hkv rows; every row is one 16-byte load and store per lane.  q goes
+//     to a head-major workspace [B][Hq][T][256] (one 3-D TMA box per 128-query tile), k and v
+//     to the caches.  It also zeroes the attention kernel's scheduler counters.
+//  2. attention: a persistent kernel, one CTA per SM, pulling work items (128-query tile x q
+//     head) from an atomic counter, heaviest tiles first (items are ordered by query tile,
+//     last first).  Per CTA, 8 warps:
+//       warp 0  scheduler + TMA producer: Q tile (64 KB) per item, then K and V as 64-key
+//               half tiles (32 KB) through a 5-slot ring; 3-D tensor maps end at pos0+T, so
+//               keys past the valid cache read as zeros, never as uninitialised memory.
+//       warp 1  TMEM owner (512 columns) and tcgen05.mma issuer (one thread):
+//               S_g = Q K_g^T (M=128, N=64 x 2, K=16 x 16) into TMEM buffer g%2;
+//               O += P_g V_g  (M=128, N=256, K=16 x 8) with P read from TMEM (the .kind::f16
+//               A-from-TMEM form) and V the MN-major B operand in shared memory.
+//               S_{g+1} is issued before PV_g, and the next item's S MMAs run while the
+//               current item's epilogue drains O.
+//       warps 4-7  softmax + epilogue, one query row per thread (TMEM lane = row): S row via
+//               tcgen05.ld, causal/window mask only on tiles that cross the band, online
 //               softmax in the log2 domain with lazy rescaling (O is rescaled in TMEM only
-//               when the row max grows by more than 2^8), P written as bf16 into shared memory
-//               in the 128-byte-swizzled K-major layout the PV MMA reads.
-//     TMEM: O = columns [0, 256), S0 = [256, 384), S1 = [384, 512).
-//     Tiles of 128 keys; only tiles that intersect the causal/window band are visited.
+//               when a row max grows by more than 2^8), P packed to bf16 and stored with
+//               tcgen05.st over the first 64 columns of its own S buffer.
+//     TMEM: O = columns [0, 256), S0/P0 = [256, 384), S1/P1 = [384, 512).
 #include <algorithm>
 
 #include "common.cuh"
@@ -35,39 +39,65 @@ namespace apex {
 namespace {
 
 constexpr int kD = 256;
-constexpr int kBM = 128;                          // queries per CTA
-constexpr int kBN = 128;                          // keys per tile
-constexpr int kSlotKeys = 64;                     // keys per ring slot
-constexpr int kSlots = 4;
-constexpr uint32_t kQChunk = kBM * 128;           // 64 dims of 128 rows, 128 B per row
-constexpr uint32_t kSlotChunk = kSlotKeys * 128;  // 64 dims of 64 keys
-constexpr uint32_t kPChunk = kBM * 128;           // 64 keys of 128 rows
-constexpr uint32_t kQBytes = kBM * kD * 2;        // 65536
+constexpr int kBM = 128;                             // queries per item
+constexpr int kBN = 128;                             // keys per tile
+constexpr int kSlotKeys = 64;                        // keys per ring slot
+constexpr int kSlots = 5;
+constexpr uint32_t kQChunk = kBM * 128;              // 64 dims x 128 rows, 128 B per row
+constexpr uint32_t kSlotChunk = kSlotKeys * 128;     // 64 dims x 64 keys
+constexpr uint32_t kQBytes = kBM * kD * 2;           // 65536
 constexpr uint32_t kSlotBytes = kSlotKeys * kD * 2;  // 32768
-constexpr uint32_t kPBytes = kBM * kBN * 2;       // 32768
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffSlots = kOffQ + kQBytes;
-constexpr uint32_t kOffP = kOffSlots + kSlots * kSlotBytes;
-constexpr uint32_t kOffBar = kOffP + kPBytes;
-constexpr uint32_t kOffTmem = kOffBar + 128;
-constexpr uint32_t kSmemBytes = kOffTmem + 128 + 1024;  // + slack to align the base to 1024
+constexpr uint32_t kOffBar = kOffSlots + kSlots * kSlotBytes;
+constexpr uint32_t kNumBars = 32;
+constexpr uint32_t kOffItems = kOffBar + 8 * kNumBars;
+constexpr uint32_t kItemRing = 8;
+constexpr uint32_t kOffTmem = kOffItems + 4 * kItemRing;
+constexpr uint32_t kSmemBytes = kOffTmem + 16 + 1024;  // + slack to align the base to 1024
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0, kColS = 256;
 constexpr int kThreads = 256;
-constexpr float kTau = 8.0f;                      // lazy-rescale threshold (log2 units)
+constexpr float kTau = 8.0f;                         // lazy-rescale threshold (log2 units)
 constexpr float kLog2e = 1.4426950408889634f;
 
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // barrier indices (8 bytes each at kOffBar)
-constexpr int kBarQ = 0, kBarFull = 1, kBarEmpty = 5, kBarS = 9, kBarP = 11, kBarO = 12;
+constexpr int kBarQFull = 0, kBarQEmpty = 1, kBarFull = 2, kBarEmpty = kBarFull + kSlots,
+              kBarS = kBarEmpty + kSlots, kBarP = kBarS + 2, kBarO = kBarP + 2, kBarOFree = kBarO + 1,
+              kBarItem = kBarOFree + 1;
+static_assert(kBarItem + kItemRing <= kNumBars, "barrier budget");
 
 struct PrefillArgs {
-    uint16_t *out;  // [B][T][Hq][D]
-    unsigned *status;  // device status word
-    uint32_t T, pos0, q_heads, kv_heads, window, n_qtiles;
+    uint16_t *out;        // [B][T][Hq][D]
+    unsigned *status;     // device status word
+    unsigned *sched;      // [0] next item, [1] CTAs done (zeroed by the prep kernel)
+    uint32_t batch, T, pos0, q_heads, kv_heads, window, n_qtiles, n_items;
     float scale_log2;
 };
+
+struct Item {
+    uint32_t b, h, kvh, t0, rows_valid, pos_first, pos_last, j_start, n_tiles;
+};
+
+__device__ __forceinline__ Item item_geometry(uint32_t idx, const PrefillArgs &a) {
+    Item it;
+    const uint32_t bh_count = a.batch * a.q_heads;
+    const uint32_t qt = a.n_qtiles - 1 - idx / bh_count;  // last query tiles (most keys) first
+    const uint32_t bh = idx % bh_count;
+    it.b = bh / a.q_heads;
+    it.h = bh % a.q_heads;
+    it.kvh = it.h / (a.q_heads / a.kv_heads);
+    it.t0 = qt * kBM;
+    it.rows_valid = min(static_cast<uint32_t>(kBM), a.T - it.t0);
+    it.pos_first = a.pos0 + it.t0;
+    it.pos_last = it.pos_first + it.rows_valid - 1;
+    const uint32_t kv_lo = (a.window && it.pos_first + 1 > a.window) ? it.pos_first + 1 - a.window : 0;
+    it.j_start = (kv_lo / kBN) * kBN;
+    it.n_tiles = (it.pos_last - it.j_start) / kBN + 1;
+    return it;
+}
 
 __device__ __forceinline__ bool visible(uint32_t key, uint32_t pos, uint32_t window) {
     return key <= pos && (window == 0 || key + window > pos);
@@ -80,30 +110,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sb = smem_u32(base);
     auto bar = [&](int i) { return sb + kOffBar + 8u * i; };
+    volatile int *items = reinterpret_cast<volatile int *>(base + kOffItems);
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(base + kOffTmem);
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t bh = blockIdx.x;
-    const uint32_t h = bh % a.q_heads, b = bh / a.q_heads;
-    const uint32_t kvh = h / (a.q_heads / a.kv_heads);
-    const uint32_t qt = a.n_qtiles - 1 - blockIdx.y;  // heaviest tiles first
-    const uint32_t t0 = qt * kBM;
-    const uint32_t rows_valid = min(static_cast<uint32_t>(kBM), a.T - t0);
-    const uint32_t pos_first = a.pos0 + t0, pos_last = pos_first + rows_valid - 1;
-    const uint32_t kv_lo = (a.window && pos_first + 1 > a.window) ? pos_first + 1 - a.window : 0;
-    const uint32_t j_start = (kv_lo / kBN) * kBN;
-    const uint32_t n_tiles = (pos_last - j_start) / kBN + 1;
 
     if (tid == 0) {
-        mbar_init(bar(kBarQ), 1);
+        mbar_init(bar(kBarQFull), 1);
+        mbar_init(bar(kBarQEmpty), 1);
         for (int i = 0; i < kSlots; ++i) {
             mbar_init(bar(kBarFull + i), 1);
             mbar_init(bar(kBarEmpty + i), 1);
         }
-        mbar_init(bar(kBarS + 0), 1);
-        mbar_init(bar(kBarS + 1), 1);
-        mbar_init(bar(kBarP), kBM);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bar(kBarS + i), 1);
+            mbar_init(bar(kBarP + i), kBM);
+        }
         mbar_init(bar(kBarO), 1);
+        mbar_init(bar(kBarOFree), kBM);
+        for (uint32_t i = 0; i < kItemRing; ++i) mbar_init(bar(kBarItem + i), 1);
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -116,33 +141,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_holder;
 
     if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer
+        // ------------------------------------------------------------ scheduler + TMA producer
         if (lane == 0) {
             prefetch_tensormap(&tm_q);
             prefetch_tensormap(&tm_k);
             prefetch_tensormap(&tm_v);
-            mbar_arrive_expect_tx(bar(kBarQ), kQBytes);
-            for (int c = 0; c < 4; ++c)
-                tma_load_3d(sb + kOffQ + c * kQChunk, &tm_q, c * 64, static_cast<int32_t>(t0),
-                            static_cast<int32_t>(b * a.q_heads + h), bar(kBarQ));
-            uint32_t n = 0;
+            uint32_t kv_n = 0;
             bool alive = true;
-            for (uint32_t j = 0; j < n_tiles && alive; ++j) {
-                const uint32_t key0 = j_start + j * kBN;
-                for (int which = 0; which < 2 && alive; ++which) {
-                    const CUtensorMap *map = which == 0 ? &tm_k : &tm_v;
-                    for (int half = 0; half < 2; ++half, ++n) {
-                        const uint32_t slot = n % kSlots;
-                        if (n >= kSlots && !mbar_wait(bar(kBarEmpty + slot), ((n / kSlots) - 1) & 1, a.status)) {
+            for (uint32_t it = 0;; ++it) {
+                int idx = static_cast<int>(atomicAdd(a.sched, 1u));
+                if (static_cast<uint32_t>(idx) >= a.n_items || !alive) idx = -1;
+                if (it >= 1 && !mbar_wait(bar(kBarQEmpty), (it - 1) & 1, a.status)) idx = -1;
+                items[it % kItemRing] = idx;
+                mbar_arrive(bar(kBarItem + it % kItemRing));
+                if (idx < 0) {
+                    mbar_arrive(bar(kBarQFull));  // releases the MMA thread with the end marker
+                    break;
+                }
+                const Item g = item_geometry(static_cast<uint32_t>(idx), a);
+                mbar_arrive_expect_tx(bar(kBarQFull), kQBytes);
+                for (int c = 0; c < 4; ++c)
+                    tma_load_3d(sb + kOffQ + c * kQChunk, &tm_q, c * 64, static_cast<int32_t>(g.t0),
+                                static_cast<int32_t>(g.b * a.q_heads + g.h), bar(kBarQFull));
+                for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
+                    const uint32_t key0 = g.j_start + j * kBN;
+                    for (int q4 = 0; q4 < 4; ++q4, ++kv_n) {  // K half 0, K half 1, V half 0, V half 1
+                        const uint32_t slot = kv_n % kSlots;
+                        if (kv_n >= kSlots &&
+                            !mbar_wait(bar(kBarEmpty + slot), ((kv_n / kSlots) - 1) & 1, a.status)) {
                             alive = false;
                             break;
                         }
                         mbar_arrive_expect_tx(bar(kBarFull + slot), kSlotBytes);
                         const uint32_t dst = sb + kOffSlots + slot * kSlotBytes;
+                        const CUtensorMap *map = q4 < 2 ? &tm_k : &tm_v;
                         for (int c = 0; c < 4; ++c)
                             tma_load_3d(dst + c * kSlotChunk, map, c * 64,
-                                        static_cast<int32_t>(key0 + half * kSlotKeys),
-                                        static_cast<int32_t>(b * a.kv_heads + kvh), bar(kBarFull + slot));
+                                        static_cast<int32_t>(key0 + (q4 & 1) * kSlotKeys),
+                                        static_cast<int32_t>(g.b * a.kv_heads + g.kvh), bar(kBarFull + slot));
                     }
                 }
             }
@@ -152,144 +188,162 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             constexpr uint32_t idS = idesc_bf16_f32(kBM, kSlotKeys, 0, 0);
             constexpr uint32_t idPV = idesc_bf16_f32(kBM, kD, 0, 1);
-            bool alive = mbar_wait(bar(kBarQ), 0, a.status);
-            auto issue_pv = [&](uint32_t i) {
+            uint32_t gt = 0, kv_n = 0;
+            bool alive = true;
+            auto wait_full = [&](uint32_t n) { return mbar_wait(bar(kBarFull + n % kSlots), (n / kSlots) & 1, a.status); };
+            // O += P_t V_t for global tile t, V at ring positions nv, nv+1
+            auto issue_pv = [&](uint32_t t, uint32_t nv, bool first, uint32_t it) {
                 if (!alive) return;
-                alive = mbar_wait(bar(kBarP), i & 1, a.status) && mbar_wait(bar(kBarFull + 2), i & 1, a.status) &&
-                        mbar_wait(bar(kBarFull + 3), i & 1, a.status);
+                alive = mbar_wait(bar(kBarP + (t & 1)), (t >> 1) & 1, a.status);
+                if (alive && first && it >= 1) alive = mbar_wait(bar(kBarOFree), (it - 1) & 1, a.status);
+                alive = alive && wait_full(nv) && wait_full(nv + 1);
                 if (!alive) return;
                 tc_fence_after();
+                const uint32_t p_col = tmem + kColS + (t & 1) * 128;
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
-                    const uint64_t ad = smem_desc_sw128(sb + kOffP + (ks / 4) * kPChunk + (ks % 4) * 32, 16, 1024);
-                    const uint32_t vslot = 2 + ks / 4;
-                    const uint64_t bd = smem_desc_sw128(sb + kOffSlots + vslot * kSlotBytes + (ks % 4) * 2048,
-                                                        kSlotChunk, 1024);
-                    tc_mma_ss(tmem + kColO, ad, bd, idPV, (i > 0 || ks > 0) ? 1u : 0u);
+                    const uint32_t vslot = (nv + ks / 4) % kSlots;
+                    const uint64_t bd =
+                        smem_desc_sw128(sb + kOffSlots + vslot * kSlotBytes + (ks % 4) * 2048, kSlotChunk, 1024);
+                    tc_mma_ts(tmem + kColO, p_col + ks * 8, bd, idPV, (!first || ks > 0) ? 1u : 0u);
                 }
                 tc_commit(bar(kBarO));
-                tc_commit(bar(kBarEmpty + 2));
-                tc_commit(bar(kBarEmpty + 3));
+                tc_commit(bar(kBarEmpty + nv % kSlots));
+                tc_commit(bar(kBarEmpty + (nv + 1) % kSlots));
             };
-            for (uint32_t j = 0; j < n_tiles && alive; ++j) {
-                alive = mbar_wait(bar(kBarFull + 0), j & 1, a.status) && mbar_wait(bar(kBarFull + 1), j & 1, a.status);
-                if (!alive) break;
+            for (uint32_t it = 0; alive; ++it) {
+                if (!mbar_wait(bar(kBarQFull), it & 1, a.status)) break;
+                const int idx = items[it % kItemRing];
+                if (idx < 0) break;
                 tc_fence_after();
-                const uint32_t s_col = kColS + (j & 1) * 128;
+                const Item g = item_geometry(static_cast<uint32_t>(idx), a);
+                for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
+                    const uint32_t t = gt + j, nk = kv_n + 4 * j;
+                    alive = wait_full(nk) && wait_full(nk + 1);
+                    if (!alive) break;
+                    tc_fence_after();
+                    const uint32_t s_col = tmem + kColS + (t & 1) * 128;
 #pragma unroll
-                for (int ks = 0; ks < 16; ++ks) {
-                    const uint64_t ad = smem_desc_sw128(sb + kOffQ + (ks / 4) * kQChunk + (ks % 4) * 32, 16, 1024);
+                    for (int ks = 0; ks < 16; ++ks) {
+                        const uint64_t ad =
+                            smem_desc_sw128(sb + kOffQ + (ks / 4) * kQChunk + (ks % 4) * 32, 16, 1024);
 #pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        const uint64_t bd = smem_desc_sw128(
-                            sb + kOffSlots + half * kSlotBytes + (ks / 4) * kSlotChunk + (ks % 4) * 32, 16, 1024);
-                        tc_mma_ss(tmem + s_col + half * kSlotKeys, ad, bd, idS, ks > 0 ? 1u : 0u);
+                        for (int half = 0; half < 2; ++half) {
+                            const uint32_t slot = (nk + half) % kSlots;
+                            const uint64_t bd = smem_desc_sw128(
+                                sb + kOffSlots + slot * kSlotBytes + (ks / 4) * kSlotChunk + (ks % 4) * 32, 16, 1024);
+                            tc_mma_ss(s_col + half * kSlotKeys, ad, bd, idS, ks > 0 ? 1u : 0u);
+                        }
                     }
+                    tc_commit(bar(kBarS + (t & 1)));
+                    tc_commit(bar(kBarEmpty + nk % kSlots));
+                    tc_commit(bar(kBarEmpty + (nk + 1) % kSlots));
+                    if (j + 1 == g.n_tiles) tc_commit(bar(kBarQEmpty));  // Q is free once these finish
+                    if (j >= 1) issue_pv(t - 1, kv_n + 4 * (j - 1) + 2, j - 1 == 0, it);
                 }
-                tc_commit(bar(kBarS + (j & 1)));
-                tc_commit(bar(kBarEmpty + 0));
-                tc_commit(bar(kBarEmpty + 1));
-                if (j >= 1) issue_pv(j - 1);
+                issue_pv(gt + g.n_tiles - 1, kv_n + 4 * (g.n_tiles - 1) + 2, g.n_tiles == 1, it);
+                gt += g.n_tiles;
+                kv_n += 4 * g.n_tiles;
             }
-            issue_pv(n_tiles - 1);
         }
     } else if (warp >= 4) {
         // ------------------------------------------------------------ softmax + epilogue
-        const uint32_t r = tid - 128;              // query row == TMEM lane
+        const uint32_t r = tid - 128;                          // query row == TMEM lane
         const uint32_t lane_base = tmem + ((32u * (warp - 4)) << 16);
-        const uint32_t t = t0 + r;
-        const uint32_t pos = a.pos0 + t;
-        const bool row_valid = r < rows_valid;
-        float m_run = -INFINITY, l_run = 0.f;
+        uint32_t gt = 0, o_seen = 0;
         bool alive = true;
-        for (uint32_t j = 0; j < n_tiles; ++j) {
-            if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarS + (j & 1)), (j >> 1) & 1, a.status))) {
-                alive = false;  // warp-uniform: the tcgen05.ld below is warp-collective
+        // observe o_done completions in order up to global tile `upto` (inclusive)
+        auto wait_o = [&](int64_t upto) {
+            while (alive && static_cast<int64_t>(o_seen) <= upto)
+                alive = __all_sync(0xffffffffu, mbar_wait(bar(kBarO), o_seen++ & 1, a.status));
+        };
+        for (uint32_t it = 0; alive; ++it) {
+            if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarItem + it % kItemRing), (it / kItemRing) & 1, a.status)))
                 break;
-            }
-            tc_fence_after();
-            uint32_t sv[4][32];
-            const uint32_t s_addr = lane_base + kColS + (j & 1) * 128;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, sv[c]);
-            tc_wait_ld();
-            const uint32_t key0 = j_start + j * kBN;
-            const bool need_mask = (key0 + kBN - 1 > pos_first) || (a.window && key0 + a.window <= pos_last);
-            float mt = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    float x = __uint_as_float(sv[c][i]) * a.scale_log2;
-                    if (need_mask && !visible(key0 + c * 32 + i, pos, a.window)) x = -INFINITY;
-                    sv[c][i] = __float_as_uint(x);
-                    mt = fmaxf(mt, x);
+            const int idx = items[it % kItemRing];
+            if (idx < 0) break;
+            const Item g = item_geometry(static_cast<uint32_t>(idx), a);
+            const uint32_t t = g.t0 + r;
+            const uint32_t pos = a.pos0 + t;
+            float m_run = -INFINITY, l_run = 0.f;
+            for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
+                const uint32_t tt = gt + j;
+                if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarS + (tt & 1)), (tt >> 1) & 1, a.status))) {
+                    alive = false;
+                    break;
                 }
-            float alpha = 1.f;
-            bool rescale = false;
-            if (mt > m_run + kTau) {
-                alpha = fast_exp2(m_run - mt);  // 0 when m_run = -inf
-                rescale = j > 0;
-                m_run = mt;
-            }
-            const float m_use = m_run == -INFINITY ? 0.f : m_run;
-            float rowsum = 0.f;
-            uint32_t packed[4][16];
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float p0 = fast_exp2(__uint_as_float(sv[c][2 * i]) - m_use);
-                    const float p1 = fast_exp2(__uint_as_float(sv[c][2 * i + 1]) - m_use);
-                    rowsum += p0 + p1;
-                    packed[c][i] = pack_bf16(p0, p1);
-                }
-            l_run = l_run * alpha + rowsum;
-            if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(bar(kBarO), (j - 1) & 1, a.status))) {
-                alive = false;
-                break;
-            }
-            // tcgen05.ld/st are warp-collective: the whole warp rescales if any of its rows
-            // must, with factor 1 for the rows that need not.
-            if (__any_sync(0xffffffffu, rescale)) {
-                const float f = rescale ? alpha : 1.0f;
                 tc_fence_after();
+                uint32_t sv[4][32];
+                const uint32_t s_addr = lane_base + kColS + (tt & 1) * 128;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, sv[c]);
+                tc_wait_ld();
+                const uint32_t key0 = g.j_start + j * kBN;
+                const bool need_mask = (key0 + kBN - 1 > g.pos_first) || (a.window && key0 + a.window <= g.pos_last);
+                float mt = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        float x = __uint_as_float(sv[c][i]) * a.scale_log2;
+                        if (need_mask && !visible(key0 + c * 32 + i, pos, a.window)) x = -INFINITY;
+                        sv[c][i] = __float_as_uint(x);
+                        mt = fmaxf(mt, x);
+                    }
+                float alpha = 1.f;
+                bool rescale = false;
+                if (mt > m_run + kTau) {
+                    alpha = fast_exp2(m_run - mt);  // 0 when m_run = -inf
+                    rescale = j > 0;
+                    m_run = mt;
+                }
+                const float m_use = m_run == -INFINITY ? 0.f : m_run;
+                float rowsum = 0.f;
+                uint32_t packed[2][32];
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float p0 = fast_exp2(__uint_as_float(sv[c][2 * i]) - m_use);
+                        const float p1 = fast_exp2(__uint_as_float(sv[c][2 * i + 1]) - m_use);
+                        rowsum += p0 + p1;
+                        packed[c >> 1][(c & 1) * 16 + i] = pack_bf16(p0, p1);
+                    }
+                l_run = l_run * alpha + rowsum;
+                // PV of the previous tile must be done before O is rescaled; waiting for it here,
+                // before P(tt) is released, also keeps every o_done wait exactly one phase
+                // ahead (PV(tt) cannot start before this thread arrives on p_full below).
+                wait_o(static_cast<int64_t>(tt) - 1);
+                if (!alive) break;
+                // tcgen05.ld/st are warp-collective: the whole warp rescales if any row must.
+                if (__any_sync(0xffffffffu, rescale)) {
+                    tc_fence_after();
+                    const float f = rescale ? alpha : 1.0f;
 #pragma unroll 1
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t o[32];
-                    tmem_ld32(lane_base + kColO + c * 32, o);
-                    tc_wait_ld();
+                    for (int c = 0; c < 8; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32(lane_base + kColO + c * 32, o);
+                        tc_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-                    tmem_st32(lane_base + kColO + c * 32, o);
+                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+                        tmem_st32(lane_base + kColO + c * 32, o);
+                    }
                 }
+                // P (bf16 pairs) over the first 64 columns of this tile's S buffer
+                tmem_st32(s_addr, packed[0]);
+                tmem_st32(s_addr + 32, packed[1]);
                 tc_wait_st();
+                tc_fence_before();
+                mbar_arrive(bar(kBarP + (tt & 1)));
             }
-            // P row r -> 128-byte-swizzled K-major tile: 16-byte unit u of key chunk c at
-            // chunk + r*128 + ((u ^ (r & 7)) * 16).
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint8_t *rowp = base + kOffP + c * kPChunk + r * 128;
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int w0 = (c * 64 + u * 8) / 2;  // packed index of the unit's first pair
-                    uint4 v;
-                    v.x = packed[w0 / 16][w0 % 16];
-                    v.y = packed[(w0 + 1) / 16][(w0 + 1) % 16];
-                    v.z = packed[(w0 + 2) / 16][(w0 + 2) % 16];
-                    v.w = packed[(w0 + 3) / 16][(w0 + 3) % 16];
-                    *reinterpret_cast<uint4 *>(rowp + ((u ^ (r & 7)) * 16)) = v;
-                }
-            }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            mbar_arrive(bar(kBarP));
-        }
-        // epilogue: O / l -> bf16 out[b][t][h][:]
-        if (__all_sync(0xffffffffu, alive && mbar_wait(bar(kBarO), (n_tiles - 1) & 1, a.status))) {
+            if (!alive) break;
+            // epilogue: O / l -> bf16 out[b][t][h][:]
+            wait_o(static_cast<int64_t>(gt + g.n_tiles) - 1);
+            if (!alive) break;
             tc_fence_after();
             const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
-            uint16_t *orow = a.out + ((static_cast<uint64_t>(b) * a.T + t) * a.q_heads + h) * kD;
+            const bool row_valid = r < g.rows_valid;
+            uint16_t *orow = a.out + ((static_cast<uint64_t>(g.b) * a.T + t) * a.q_heads + g.h) * kD;
 #pragma unroll 1
             for (int c = 0; c < 8; ++c) {
                 uint32_t o[32];
@@ -308,6 +362,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+            tc_fence_before();
+            mbar_arrive(bar(kBarOFree));
+            gt += g.n_tiles;
         }
     }
     tc_fence_before();
@@ -316,76 +373,121 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+    if (tid == 0) {
+        // the last CTA to finish resets the scheduler for the next launch
+        __threadfence();
+        if (atomicAdd(a.sched + 1, 1u) == gridDim.x - 1) {
+            a.sched[0] = 0;
+            a.sched[1] = 0;
+        }
+    }
 }
 
 // ---------------------------------------------------------------- prep: norm + rope + append
 struct PrepArgs {
     const uint16_t *q_raw, *k_raw, *v_raw, *q_w, *k_w;
     uint16_t *q_ws, *k_cache, *v_cache;
+    unsigned *sched;
     uint32_t B, T, pos0, q_heads, kv_heads, capacity, rope_pairs, qk_norm, v_norm;
-    float rope_base, eps;
+    float eps;
+    RopeTable rope;
 };
 
-__global__ void __launch_bounds__(256) prefill_prep_kernel(const PrepArgs a) {
-    __shared__ float inv_freq[kD / 2];
-    for (uint32_t i = threadIdx.x; i < a.rope_pairs; i += blockDim.x)
-        inv_freq[i] = rope_inv_freq(i, kD, a.rope_base);
-    __syncthreads();
-    const uint32_t lane = threadIdx.x & 31;
-    const uint64_t nq = static_cast<uint64_t>(a.B) * a.T * a.q_heads;
-    const uint64_t nk = static_cast<uint64_t>(a.B) * a.T * a.kv_heads;
-    const uint64_t total = nq + 2 * nk;
-    const uint64_t warps = static_cast<uint64_t>(gridDim.x) * (blockDim.x >> 5);
-    for (uint64_t r = static_cast<uint64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < total;
-         r += warps) {
-        const uint16_t *src;
-        uint16_t *dst;
-        const uint16_t *w;
-        bool norm;
-        uint32_t pairs, t;
-        if (r < nq) {
-            const uint32_t hq = static_cast<uint32_t>(r % a.q_heads);
-            const uint64_t bt = r / a.q_heads;
-            t = static_cast<uint32_t>(bt % a.T);
-            const uint32_t bb = static_cast<uint32_t>(bt / a.T);
-            src = a.q_raw + r * kD;
-            dst = a.q_ws + ((static_cast<uint64_t>(bb) * a.q_heads + hq) * a.T + t) * kD;
-            w = a.q_w;
-            norm = a.qk_norm;
-            pairs = a.rope_pairs;
-        } else {
-            const bool is_k = r < nq + nk;
-            const uint64_t rr = r - nq - (is_k ? 0 : nk);
-            const uint32_t hk = static_cast<uint32_t>(rr % a.kv_heads);
-            const uint64_t bt = rr / a.kv_heads;
-            t = static_cast<uint32_t>(bt % a.T);
-            const uint32_t bb = static_cast<uint32_t>(bt / a.T);
-            src = (is_k ? a.k_raw : a.v_raw) + rr * kD;
-            dst = (is_k ? a.k_cache : a.v_cache) +
-                  ((static_cast<uint64_t>(bb) * a.kv_heads + hk) * a.capacity + a.pos0 + t) * kD;
-            w = is_k ? a.k_w : nullptr;
-            norm = is_k ? a.qk_norm : a.v_norm;
-            pairs = is_k ? a.rope_pairs : 0;
+// RMSNorm (optional, weight in registers) + RoPE with this lane's precomputed cos/sin of one
+// 256-wide row held 8 dims per lane; pairs (i, i+128) meet across lanes l and l^16.
+__device__ __forceinline__ void norm_rope_cs(float (&x)[8], uint32_t lane, bool norm, const float (&w)[8],
+                                             float eps, bool rope, uint32_t rope_pairs, const float (&cs)[8],
+                                             const float (&sn)[8]) {
+    if (norm) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / sqrtf(ss / static_cast<float>(kD) + eps);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = x[e] * inv * w[e];
+    }
+    if (rope) {
+        const bool low = lane < 16;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
+            if (8 * (lane & 15) + e < rope_pairs)
+                x[e] = low ? (x[e] * cs[e] - other * sn[e]) : (other * sn[e] + x[e] * cs[e]);
         }
-        float x[8];
-        unpack8(*reinterpret_cast<const uint4 *>(src + 8 * lane), x);
-        norm_rope_row(x, lane, norm, w, a.eps, pairs, inv_freq, static_cast<float>(a.pos0 + t));
-        *reinterpret_cast<uint4 *>(dst + 8 * lane) = pack8(x);
     }
 }
+
+__global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant__ PrepArgs a) {
+    const uint32_t lane = threadIdx.x & 31;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        a.sched[0] = 0;
+        a.sched[1] = 0;
+    }
+    float qw[8], kw[8], ones[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        qw[e] = a.q_w ? __uint_as_float(static_cast<uint32_t>(a.q_w[8 * lane + e]) << 16) : 1.0f;
+        kw[e] = a.k_w ? __uint_as_float(static_cast<uint32_t>(a.k_w[8 * lane + e]) << 16) : 1.0f;
+        ones[e] = 1.0f;
+    }
+    const uint64_t positions = static_cast<uint64_t>(a.B) * a.T;
+    const uint64_t warps = static_cast<uint64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (uint64_t bt = static_cast<uint64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); bt < positions;
+         bt += warps) {
+        const uint32_t b = static_cast<uint32_t>(bt / a.T), t = static_cast<uint32_t>(bt % a.T);
+        const float pos = static_cast<float>(a.pos0 + t);
+        float cs[8], sn[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const uint32_t i = 8 * (lane & 15) + e;
+            if (i < a.rope_pairs) sincos_angle(pos * a.rope.inv_freq[i], sn[e], cs[e]);
+            else cs[e] = 1.f, sn[e] = 0.f;
+        }
+        // q rows -> workspace (head-major)
+        const uint16_t *qsrc = a.q_raw + bt * a.q_heads * kD;
+        for (uint32_t h = 0; h < a.q_heads; ++h) {
+            float x[8];
+            unpack8(*reinterpret_cast<const uint4 *>(qsrc + h * kD + 8 * lane), x);
+            norm_rope_cs(x, lane, a.qk_norm, qw, a.eps, a.rope_pairs != 0, a.rope_pairs, cs, sn);
+            uint16_t *dst = a.q_ws + ((static_cast<uint64_t>(b) * a.q_heads + h) * a.T + t) * kD;
+            *reinterpret_cast<uint4 *>(dst + 8 * lane) = pack8(x);
+        }
+        // k and v rows -> caches at position pos0 + t
+        const uint16_t *ksrc = a.k_raw + bt * a.kv_heads * kD;
+        const uint16_t *vsrc = a.v_raw + bt * a.kv_heads * kD;
+        for (uint32_t h = 0; h < a.kv_heads; ++h) {
+            const uint64_t off = ((static_cast<uint64_t>(b) * a.kv_heads + h) * a.capacity + a.pos0 + t) * kD;
+            float x[8], y[8];
+            unpack8(*reinterpret_cast<const uint4 *>(ksrc + h * kD + 8 * lane), x);
+            unpack8(*reinterpret_cast<const uint4 *>(vsrc + h * kD + 8 * lane), y);
+            norm_rope_cs(x, lane, a.qk_norm, kw, a.eps, a.rope_pairs != 0, a.rope_pairs, cs, sn);
+            norm_rope_cs(y, lane, a.v_norm, ones, a.eps, false, 0, cs, sn);
+            *reinterpret_cast<uint4 *>(a.k_cache + off + 8 * lane) = pack8(x);
+            *reinterpret_cast<uint4 *>(a.v_cache + off + 8 * lane) = pack8(y);
+        }
+    }
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 size_t q_ws_bytes(uint32_t batch, uint32_t tokens, uint32_t q_heads) {
     return static_cast<size_t>(batch) * tokens * q_heads * kD * 2;
 }
 
-}  // namespace
-}  // namespace apex
+size_t ws_bytes(uint32_t batch, uint32_t tokens, uint32_t q_heads) {
+    return align256(q_ws_bytes(batch, tokens, q_heads)) + 256;  // + scheduler counters
+}
 
-namespace apex {
-namespace {
+unsigned *sched_ptr(void *workspace, uint32_t batch, uint32_t tokens, uint32_t q_heads) {
+    return reinterpret_cast<unsigned *>(static_cast<uint8_t *>(workspace) +
+                                        align256(q_ws_bytes(batch, tokens, q_heads)));
+}
 
 int validate_prefill(const apex_attn_params *p, uint32_t capacity, uint32_t batch, uint32_t tokens,
-                     uint32_t pos0, std::initializer_list<const void *> tensors, const char *name) {
+                     uint32_t pos0, std::initializer_list<const void *> tensors, void *workspace,
+                     size_t workspace_bytes, const char *name) {
     const std::string n(name);
     if (!p) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": null params");
     if (p->head_dim != kD) return fail(APEX_ERR_UNSUPPORTED, n + ": this build supports head_dim 256");
@@ -399,28 +501,38 @@ int validate_prefill(const apex_attn_params *p, uint32_t capacity, uint32_t batc
     }
     if (static_cast<uint64_t>(pos0) + tokens > capacity)
         return fail(APEX_ERR_INVALID_ARGUMENT, n + ": pos0 + tokens exceeds capacity");
-    if ((tokens + kBM - 1) / kBM > 65535 || static_cast<uint64_t>(batch) * p->q_heads > 0x7fffffffu)
-        return fail(APEX_ERR_INVALID_ARGUMENT, n + ": problem too large for one launch");
+    const uint64_t items = static_cast<uint64_t>(batch) * p->q_heads * ((tokens + kBM - 1) / kBM);
+    if (items > 0x7fffffffull) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": problem too large for one launch");
+    const size_t need = ws_bytes(batch, tokens, p->q_heads);
+    if (!workspace || workspace_bytes < need)
+        return fail(APEX_ERR_WORKSPACE, n + ": workspace of " + std::to_string(need) + " bytes required");
+    if (!aligned16(workspace)) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": tensors must be 16-byte aligned");
     return APEX_OK;
 }
 
 int launch_prep(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t *k_raw, const uint16_t *v_raw,
                 const uint16_t *q_w, const uint16_t *k_w, uint16_t *k_cache, uint16_t *v_cache,
-                uint32_t capacity, uint32_t batch, uint32_t tokens, uint32_t pos0, uint16_t *q_normed,
+                uint32_t capacity, uint32_t batch, uint32_t tokens, uint32_t pos0, void *workspace,
                 cudaStream_t s) {
-    PrepArgs pa{q_raw, k_raw, v_raw, q_w, k_w, q_normed, k_cache, v_cache, batch, tokens, pos0, p->q_heads,
-                p->kv_heads, capacity, p->rope_pairs, p->qk_norm, p->v_norm, p->rope_base, p->eps};
-    const uint64_t rows = static_cast<uint64_t>(batch) * tokens * (p->q_heads + 2ull * p->kv_heads);
-    const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>((rows + 7) / 8, 16ull * sm_count()));
+    PrepArgs pa{};
+    pa.q_raw = q_raw; pa.k_raw = k_raw; pa.v_raw = v_raw; pa.q_w = q_w; pa.k_w = k_w;
+    pa.q_ws = static_cast<uint16_t *>(workspace); pa.k_cache = k_cache; pa.v_cache = v_cache;
+    pa.sched = sched_ptr(workspace, batch, tokens, p->q_heads);
+    pa.B = batch; pa.T = tokens; pa.pos0 = pos0; pa.q_heads = p->q_heads; pa.kv_heads = p->kv_heads;
+    pa.capacity = capacity; pa.rope_pairs = p->rope_pairs; pa.qk_norm = p->qk_norm; pa.v_norm = p->v_norm;
+    pa.eps = p->eps;
+    rope_table(pa.rope.inv_freq, p->rope_pairs, kD, p->rope_base);
+    const uint64_t positions = static_cast<uint64_t>(batch) * tokens;
+    const uint32_t grid = static_cast<uint32_t>(std::max<uint64_t>(1, std::min<uint64_t>((positions + 7) / 8, 16ull * sm_count())));
     prefill_prep_kernel<<<grid, 256, 0, s>>>(pa);
     return check_cuda(cudaGetLastError(), "prefill prep launch");
 }
 
-int launch_attend(const apex_attn_params *p, const uint16_t *q_normed, const uint16_t *k_cache,
-                  const uint16_t *v_cache, uint32_t capacity, uint32_t batch, uint32_t tokens, uint32_t pos0,
-                  uint16_t *out, cudaStream_t s) {
+int launch_attend(const apex_attn_params *p, void *workspace, const uint16_t *k_cache, const uint16_t *v_cache,
+                  uint32_t capacity, uint32_t batch, uint32_t tokens, uint32_t pos0, uint16_t *out,
+                  cudaStream_t s) {
     CUtensorMap tq, tk, tv;
-    int rc = make_tensor_map_bf16_3d(&tq, q_normed, kD, tokens, static_cast<uint64_t>(batch) * p->q_heads,
+    int rc = make_tensor_map_bf16_3d(&tq, workspace, kD, tokens, static_cast<uint64_t>(batch) * p->q_heads,
                                      kD * 2ull, static_cast<uint64_t>(tokens) * kD * 2, 64, kBM);
     if (rc) return rc;
     const uint64_t kv_len = static_cast<uint64_t>(pos0) + tokens;
@@ -440,11 +552,17 @@ int launch_attend(const apex_attn_params *p, const uint16_t *q_normed, const uin
         if (rc) return rc;
         attr_set[dev] = true;
     }
-    unsigned *status = device_status_ptr();
-    if (!status) return fail(APEX_ERR_CUDA, "prefill: device status word unavailable");
-    const uint32_t n_qtiles = (tokens + kBM - 1) / kBM;
-    PrefillArgs fa{out, status, tokens, pos0, p->q_heads, p->kv_heads, p->window, n_qtiles, p->scale * kLog2e};
-    const dim3 grid(batch * p->q_heads, n_qtiles);
+    PrefillArgs fa{};
+    fa.out = out;
+    fa.status = device_status_ptr();
+    if (!fa.status) return fail(APEX_ERR_CUDA, "prefill: device status word unavailable");
+    fa.sched = sched_ptr(workspace, batch, tokens, p->q_heads);
+    fa.batch = batch; fa.T = tokens; fa.pos0 = pos0; fa.q_heads = p->q_heads; fa.kv_heads = p->kv_heads;
+    fa.window = p->window;
+    fa.n_qtiles = (tokens + kBM - 1) / kBM;
+    fa.n_items = batch * p->q_heads * fa.n_qtiles;
+    fa.scale_log2 = p->scale * kLog2e;
+    const uint32_t grid = std::min<uint32_t>(fa.n_items, static_cast<uint32_t>(sm_count()));
     prefill_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(tq, tk, tv, fa);
     return check_cuda(cudaGetLastError(), "prefill attention launch");
 }
@@ -455,7 +573,7 @@ int launch_attend(const apex_attn_params *p, const uint16_t *q_normed, const uin
 extern "C" size_t apex_attn_prefill_workspace_bytes(const apex_attn_params *p, uint32_t batch,
                                                     uint32_t tokens) {
     if (!p) return 0;
-    return apex::q_ws_bytes(batch, tokens, p->q_heads);
+    return apex::ws_bytes(batch, tokens, p->q_heads);
 }
 
 extern "C" int apex_attn_prefill_prep_bf16(const apex_attn_params *p, const uint16_t *q_raw,
@@ -463,25 +581,26 @@ extern "C" int apex_attn_prefill_prep_bf16(const apex_attn_params *p, const uint
                                            const uint16_t *q_norm_w, const uint16_t *k_norm_w,
                                            uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
                                            uint32_t batch, uint32_t tokens, uint32_t pos0,
-                                           uint16_t *q_normed, void *stream) {
+                                           void *workspace, size_t workspace_bytes, void *stream) {
     using namespace apex;
-    int rc = validate_prefill(p, capacity, batch, tokens, pos0, {q_raw, k_raw, v_raw, k_cache, v_cache, q_normed},
-                              "apex_attn_prefill_prep_bf16");
+    int rc = validate_prefill(p, capacity, batch, tokens, pos0, {q_raw, k_raw, v_raw, k_cache, v_cache}, workspace,
+                              workspace_bytes, "apex_attn_prefill_prep_bf16");
     if (rc || batch == 0 || tokens == 0) return rc ? rc : ok();
     rc = launch_prep(p, q_raw, k_raw, v_raw, q_norm_w, k_norm_w, k_cache, v_cache, capacity, batch, tokens, pos0,
-                     q_normed, static_cast<cudaStream_t>(stream));
+                     workspace, static_cast<cudaStream_t>(stream));
     return rc ? rc : ok();
 }
 
-extern "C" int apex_attn_prefill_attend_bf16(const apex_attn_params *p, const uint16_t *q_normed,
-                                             const uint16_t *k_cache, const uint16_t *v_cache,
-                                             uint32_t capacity, uint32_t batch, uint32_t tokens,
-                                             uint32_t pos0, uint16_t *out, void *stream) {
+extern "C" int apex_attn_prefill_attend_bf16(const apex_attn_params *p, void *workspace,
+                                             size_t workspace_bytes, const uint16_t *k_cache,
+                                             const uint16_t *v_cache, uint32_t capacity,
+                                             uint32_t batch, uint32_t tokens, uint32_t pos0,
+                                             uint16_t *out, void *stream) {
     using namespace apex;
-    int rc = validate_prefill(p, capacity, batch, tokens, pos0, {q_normed, k_cache, v_cache, out},
+    int rc = validate_prefill(p, capacity, batch, tokens, pos0, {k_cache, v_cache, out}, workspace, workspace_bytes,
                               "apex_attn_prefill_attend_bf16");
     if (rc || batch == 0 || tokens == 0) return rc ? rc : ok();
-    rc = launch_attend(p, q_normed, k_cache, v_cache, capacity, batch, tokens, pos0, out,
+    rc = launch_attend(p, workspace, k_cache, v_cache, capacity, batch, tokens, pos0, out,
                        static_cast<cudaStream_t>(stream));
     return rc ? rc : ok();
 }
@@ -495,16 +614,12 @@ extern "C" int apex_attn_prefill_bf16(const apex_attn_params *p, const uint16_t 
                                       void *stream) {
     using namespace apex;
     int rc = validate_prefill(p, capacity, batch, tokens, pos0, {q_raw, k_raw, v_raw, k_cache, v_cache, out},
-                              "apex_attn_prefill_bf16");
+                              workspace, workspace_bytes, "apex_attn_prefill_bf16");
     if (rc || batch == 0 || tokens == 0) return rc ? rc : ok();
-    const size_t need = q_ws_bytes(batch, tokens, p->q_heads);
-    if (!workspace || workspace_bytes < need)
-        return fail(APEX_ERR_WORKSPACE, "apex_attn_prefill_bf16: workspace of " + std::to_string(need) + " bytes required");
-    if (!aligned16(workspace)) return fail(APEX_ERR_INVALID_ARGUMENT, "apex_attn_prefill_bf16: tensors must be 16-byte aligned");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    uint16_t *qn = static_cast<uint16_t *>(workspace);
-    rc = launch_prep(p, q_raw, k_raw, v_raw, q_norm_w, k_norm_w, k_cache, v_cache, capacity, batch, tokens, pos0, qn, s);
+    rc = launch_prep(p, q_raw, k_raw, v_raw, q_norm_w, k_norm_w, k_cache, v_cache, capacity, batch, tokens, pos0,
+                     workspace, s);
     if (rc) return rc;
-    rc = launch_attend(p, qn, k_cache, v_cache, capacity, batch, tokens, pos0, out, s);
+    rc = launch_attend(p, workspace, k_cache, v_cache, capacity, batch, tokens, pos0, out, s);
     return rc ? rc : ok();
 }

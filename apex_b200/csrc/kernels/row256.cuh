@@ -53,7 +53,7 @@ __device__ __forceinline__ void norm_rope_row(float (&x)[8], uint32_t lane, bool
             const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
             if (i < rope_pairs) {
                 float s, c;
-                sincosf(pos * inv_freq[i], &s, &c);
+                sincos_angle(pos * inv_freq[i], s, c);
                 x[e] = low ? (x[e] * c - other * s) : (other * s + x[e] * c);
             }
         }

@@ -239,24 +239,24 @@ def attention_prefill(shape: AttentionShape, q_raw, k_raw, v_raw, q_norm_w, k_no
 
 
 def attention_prefill_prep(shape: AttentionShape, q_raw, k_raw, v_raw, q_norm_w, k_norm_w,
-                           cache: KvCache, pos0: int, q_normed: torch.Tensor) -> None:
+                           cache: KvCache, pos0: int, workspace: "PrefillWorkspace") -> None:
     """First stage of attention_prefill (apex_attn_prefill_prep_bf16): norm + RoPE, K/V
-    appended to the cache, normalised q -> q_normed [B, Hq, T, D] bf16 (head-major)."""
+    appended to the cache, normalised q into the workspace."""
     B, T = q_raw.shape[0], q_raw.shape[1]
     check(_native.load().apex_attn_prefill_prep_bf16(shape.c(), q_raw.data_ptr(), k_raw.data_ptr(),
                                                      v_raw.data_ptr(), _ptr(q_norm_w), _ptr(k_norm_w),
                                                      cache.k.data_ptr(), cache.v.data_ptr(),
-                                                     cache.capacity, B, T, pos0, q_normed.data_ptr(),
-                                                     _stream()))
+                                                     cache.capacity, B, T, pos0, workspace.buffer.data_ptr(),
+                                                     workspace.nbytes, _stream()))
 
 
-def attention_prefill_attend(shape: AttentionShape, q_normed: torch.Tensor, cache: KvCache,
+def attention_prefill_attend(shape: AttentionShape, workspace: "PrefillWorkspace", cache: KvCache,
                              batch: int, tokens: int, pos0: int, out: torch.Tensor) -> None:
     """Second stage of attention_prefill (apex_attn_prefill_attend_bf16): tcgen05 attention of
-    q_normed [B, Hq, T, D] over cache positions [0, pos0 + T) -> out [B, T, Hq, D]."""
-    check(_native.load().apex_attn_prefill_attend_bf16(shape.c(), q_normed.data_ptr(), cache.k.data_ptr(),
-                                                       cache.v.data_ptr(), cache.capacity, batch, tokens,
-                                                       pos0, out.data_ptr(), _stream()))
+    the workspace's normalised q over cache positions [0, pos0 + T) -> out [B, T, Hq, D]."""
+    check(_native.load().apex_attn_prefill_attend_bf16(shape.c(), workspace.buffer.data_ptr(), workspace.nbytes,
+                                                       cache.k.data_ptr(), cache.v.data_ptr(), cache.capacity,
+                                                       batch, tokens, pos0, out.data_ptr(), _stream()))
 
 
 def device_status() -> None:

@@ -135,7 +135,7 @@ class PrefillWorkload:
         for _ in range(self.R):
             s = dict(q=randn(B, T, Hq, D), k=randn(B, T, Hkv, D), v=randn(B, T, Hkv, D),
                      kc=randn(B, Hkv, cap, D), vc=randn(B, Hkv, cap, D),
-                     qn=torch.empty(B, Hq, T, D, dtype=bf, device=device),
+                     ws=ops.PrefillWorkspace(self.shape, B, T, device=device),
                      out=torch.empty(B, T, Hq, D, dtype=bf, device=device))
             s["cache"] = ops.KvCache(s["kc"], s["vc"])
             self.sets.append(s)
@@ -148,12 +148,12 @@ class PrefillWorkload:
     def step(self, i):
         s = self.sets[i % self.R]
         self.ops.attention_prefill_prep(self.shape, s["q"], s["k"], s["v"], self.qw, self.kw, s["cache"],
-                                        self.pos0, s["qn"])
-        self.ops.attention_prefill_attend(self.shape, s["qn"], s["cache"], self.B, self.T, self.pos0, s["out"])
+                                        self.pos0, s["ws"])
+        self.ops.attention_prefill_attend(self.shape, s["ws"], s["cache"], self.B, self.T, self.pos0, s["out"])
 
     def dominant(self, i):
         s = self.sets[i % self.R]
-        self.ops.attention_prefill_attend(self.shape, s["qn"], s["cache"], self.B, self.T, self.pos0, s["out"])
+        self.ops.attention_prefill_attend(self.shape, s["ws"], s["cache"], self.B, self.T, self.pos0, s["out"])
 
     def roofline_work(self):
         return self.flops, "tensor"

@@ -176,25 +176,30 @@ APEX_API int apex_attn_decode_partial_bf16(const apex_attn_params *p, const uint
 APEX_API int apex_attn_merge_partials(const float *partials, uint32_t num_partials, uint32_t rows,
                              uint32_t head_dim, uint16_t *out, void *stream);
 
-/* Workspace bytes apex_attn_prefill_bf16 needs (the normalised, head-major Q). */
+/* Workspace bytes apex_attn_prefill_bf16 needs: the normalised, head-major Q plus 256 bytes
+ * of scheduler state for the persistent attention kernel. */
 APEX_API size_t apex_attn_prefill_workspace_bytes(const apex_attn_params *p, uint32_t batch,
                                          uint32_t tokens);
 
 /* The first stage of apex_attn_prefill_bf16 on its own: q/k norm + RoPE, K/V appended to the
- * caches at pos0, normalised q written head-major to q_normed [B][Hq][T][D] (bf16). */
+ * caches at pos0, normalised q written head-major into the workspace ([B][Hq][T][D] bf16 at its
+ * start), and the attention stage's scheduler state reset.  workspace: as for
+ * apex_attn_prefill_bf16. */
 APEX_API int apex_attn_prefill_prep_bf16(const apex_attn_params *p, const uint16_t *q_raw,
                                          const uint16_t *k_raw, const uint16_t *v_raw,
                                          const uint16_t *q_norm_w, const uint16_t *k_norm_w,
                                          uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
                                          uint32_t batch, uint32_t tokens, uint32_t pos0,
-                                         uint16_t *q_normed, void *stream);
+                                         void *workspace, size_t workspace_bytes, void *stream);
 
-/* The second stage on its own: tcgen05 attention of q_normed [B][Hq][T][D] (queries at pos0..)
- * over cache positions [0, pos0+tokens) -> out [B][T][Hq][D]. */
-APEX_API int apex_attn_prefill_attend_bf16(const apex_attn_params *p, const uint16_t *q_normed,
-                                           const uint16_t *k_cache, const uint16_t *v_cache,
-                                           uint32_t capacity, uint32_t batch, uint32_t tokens,
-                                           uint32_t pos0, uint16_t *out, void *stream);
+/* The second stage on its own: tcgen05 attention of the normalised q held in the workspace
+ * (written by apex_attn_prefill_prep_bf16 for the same batch / tokens / pos0) over cache
+ * positions [0, pos0+tokens) -> out [B][T][Hq][D].  Persistent: one CTA per SM. */
+APEX_API int apex_attn_prefill_attend_bf16(const apex_attn_params *p, void *workspace,
+                                           size_t workspace_bytes, const uint16_t *k_cache,
+                                           const uint16_t *v_cache, uint32_t capacity,
+                                           uint32_t batch, uint32_t tokens, uint32_t pos0,
+                                           uint16_t *out, void *stream);
 
 /* Causal (optionally sliding-window) prefill of `tokens` new tokens per sequence at
  * positions pos0 .. pos0+tokens-1, fused: q/k norm + RoPE, K/V appended to the caches, then
