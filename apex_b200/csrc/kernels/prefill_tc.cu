@@ -53,11 +53,12 @@ constexpr uint32_t kOffBar = kOffSlots + kSlots * kSlotBytes;
 constexpr uint32_t kNumBars = 32;
 constexpr uint32_t kOffItems = kOffBar + 8 * kNumBars;
 constexpr uint32_t kItemRing = 8;
-constexpr uint32_t kOffTmem = kOffItems + 4 * kItemRing;
-constexpr uint32_t kSmemBytes = kOffTmem + 16 + 1024;  // + slack to align the base to 1024
+constexpr uint32_t kOffRed = kOffItems + 4 * kItemRing;  // float [2 parity][2 half][128]
+constexpr uint32_t kOffTmem = kOffRed + 2 * 2 * 128 * 4;
+constexpr uint32_t kSmemBytes = kOffTmem + 16;  // the dynamic shared memory base is 1024-aligned
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0, kColS = 256;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;                          // 12 warps: 0 TMA, 1 MMA, 4-11 softmax
 constexpr float kTau = 8.0f;                         // lazy-rescale threshold (log2 units)
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -66,8 +67,8 @@ static_assert(kSmemBytes <= 232448, "shared memory budget");
 // barrier indices (8 bytes each at kOffBar)
 constexpr int kBarQFull = 0, kBarQEmpty = 1, kBarFull = 2, kBarEmpty = kBarFull + kSlots,
               kBarS = kBarEmpty + kSlots, kBarP = kBarS + 2, kBarO = kBarP + 2, kBarOFree = kBarO + 1,
-              kBarItem = kBarOFree + 1;
-static_assert(kBarItem + kItemRing <= kNumBars, "barrier budget");
+              kBarItem = kBarOFree + 1, kBarRed = kBarItem + kItemRing;
+static_assert(kBarRed + 2 <= kNumBars, "barrier budget");
 
 struct PrefillArgs {
     uint16_t *out;        // [B][T][Hq][D]
@@ -99,16 +100,16 @@ __device__ __forceinline__ Item item_geometry(uint32_t idx, const PrefillArgs &a
     return it;
 }
 
-__device__ __forceinline__ bool visible(uint32_t key, uint32_t pos, uint32_t window) {
-    return key <= pos && (window == 0 || key + window > pos);
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *base = smem_raw;
     const uint32_t sb = smem_u32(base);
+    if (sb & 1023u) {  // the swizzled tiles need 1024-byte alignment; never expected to fire
+        if (threadIdx.x == 0) atomicOr(a.status, kStatusTimeout);
+        return;
+    }
     auto bar = [&](int i) { return sb + kOffBar + 8u * i; };
     volatile int *items = reinterpret_cast<volatile int *>(base + kOffItems);
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(base + kOffTmem);
@@ -124,10 +125,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar(kBarS + i), 1);
-            mbar_init(bar(kBarP + i), kBM);
+            mbar_init(bar(kBarP + i), 2 * kBM);
+            mbar_init(bar(kBarRed + i), 2 * kBM);
         }
         mbar_init(bar(kBarO), 1);
-        mbar_init(bar(kBarOFree), kBM);
+        mbar_init(bar(kBarOFree), 2 * kBM);
         for (uint32_t i = 0; i < kItemRing; ++i) mbar_init(bar(kBarItem + i), 1);
         fence_mbar_init();
     }
@@ -248,14 +250,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 4) {
         // ------------------------------------------------------------ softmax + epilogue
-        const uint32_t r = tid - 128;                          // query row == TMEM lane
-        const uint32_t lane_base = tmem + ((32u * (warp - 4)) << 16);
-        uint32_t gt = 0, o_seen = 0;
+        // Two warpgroups share each query row: half 0 owns S columns [0, 64) and O columns
+        // [0, 128), half 1 owns S columns [64, 128) and O columns [128, 256).  The row max (every
+        // tile) and the row sum (every item) are exchanged through shared memory with an
+        // mbarrier handshake, so every wait stays bounded.
+        const uint32_t half = (warp - 4) >> 2, quad = warp & 3;
+        const uint32_t r = quad * 32 + lane;                  // query row == TMEM lane
+        const uint32_t lane_base = tmem + ((32u * quad) << 16);
+        float *red = reinterpret_cast<float *>(base + kOffRed);  // [2 parity][2 half][128]
+        uint32_t gt = 0, o_seen = 0, xchg = 0;
         bool alive = true;
         // observe o_done completions in order up to global tile `upto` (inclusive)
         auto wait_o = [&](int64_t upto) {
             while (alive && static_cast<int64_t>(o_seen) <= upto)
                 alive = __all_sync(0xffffffffu, mbar_wait(bar(kBarO), o_seen++ & 1, a.status));
+        };
+        // swap one float with the thread owning the same row in the other half
+        auto exchange = [&](float mine, float &theirs) {
+            const uint32_t slot = xchg & 1;
+            red[(slot * 2 + half) * kBM + r] = mine;
+            mbar_arrive(bar(kBarRed + slot));
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarRed + slot), (xchg >> 1) & 1, a.status));
+            theirs = red[(slot * 2 + (half ^ 1)) * kBM + r];
+            ++xchg;
+            return ok;
         };
         for (uint32_t it = 0; alive; ++it) {
             if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarItem + it % kItemRing), (it / kItemRing) & 1, a.status)))
@@ -264,32 +282,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (idx < 0) break;
             const Item g = item_geometry(static_cast<uint32_t>(idx), a);
             const uint32_t t = g.t0 + r;
-            const uint32_t pos = a.pos0 + t;
-            float m_run = -INFINITY, l_run = 0.f;
+            const int pos = static_cast<int>(a.pos0 + t);
+            float m_run = -INFINITY, l_part = 0.f;
             for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
                 const uint32_t tt = gt + j;
-                if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarS + (tt & 1)), (tt >> 1) & 1, a.status))) {
+                bool ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarS + (tt & 1)), (tt >> 1) & 1, a.status));
+                tc_fence_after();
+                uint32_t sv[2][32];
+                const uint32_t s_addr = lane_base + kColS + (tt & 1) * 128 + half * 64;
+                if (ok) {
+                    tmem_ld32(s_addr, sv[0]);
+                    tmem_ld32(s_addr + 32, sv[1]);
+                    tc_wait_ld();
+                }
+                const uint32_t tile0 = g.j_start + j * kBN;
+                const bool need_mask = (tile0 + kBN - 1 > g.pos_first) || (a.window && tile0 + a.window <= g.pos_last);
+                if (need_mask) {
+                    // visible keys of this row relative to this half's first key: [lo, hi]
+                    const int key0 = static_cast<int>(tile0 + half * 64);
+                    const int hi = pos - key0;
+                    const int lo = a.window ? pos + 1 - static_cast<int>(a.window) - key0 : -(1 << 30);
+#pragma unroll
+                    for (int k = 0; k < 64; ++k)
+                        if (k > hi || k < lo) sv[k >> 5][k & 31] = 0xff800000u;  // -inf
+                }
+                float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                for (int k = 0; k < 64; ++k) mx[k & 3] = fmaxf(mx[k & 3], __uint_as_float(sv[k >> 5][k & 31]));
+                float other;
+                ok = exchange(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), other) && ok;
+                if (!ok) {
                     alive = false;
                     break;
                 }
-                tc_fence_after();
-                uint32_t sv[4][32];
-                const uint32_t s_addr = lane_base + kColS + (tt & 1) * 128;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, sv[c]);
-                tc_wait_ld();
-                const uint32_t key0 = g.j_start + j * kBN;
-                const bool need_mask = (key0 + kBN - 1 > g.pos_first) || (a.window && key0 + a.window <= g.pos_last);
-                float mt = -INFINITY;
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        float x = __uint_as_float(sv[c][i]) * a.scale_log2;
-                        if (need_mask && !visible(key0 + c * 32 + i, pos, a.window)) x = -INFINITY;
-                        sv[c][i] = __float_as_uint(x);
-                        mt = fmaxf(mt, x);
-                    }
+                const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), other) * a.scale_log2;
                 float alpha = 1.f;
                 bool rescale = false;
                 if (mt > m_run + kTau) {
@@ -297,19 +323,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     rescale = j > 0;
                     m_run = mt;
                 }
-                const float m_use = m_run == -INFINITY ? 0.f : m_run;
-                float rowsum = 0.f;
-                uint32_t packed[2][32];
+                const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
+                float sum[4] = {0.f, 0.f, 0.f, 0.f};
+                uint32_t packed[32];
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float p0 = fast_exp2(__uint_as_float(sv[c][2 * i]) - m_use);
-                        const float p1 = fast_exp2(__uint_as_float(sv[c][2 * i + 1]) - m_use);
-                        rowsum += p0 + p1;
-                        packed[c >> 1][(c & 1) * 16 + i] = pack_bf16(p0, p1);
-                    }
-                l_run = l_run * alpha + rowsum;
+                for (int i = 0; i < 32; ++i) {
+                    const float p0 = fast_exp2(fmaf(__uint_as_float(sv[i >> 4][(2 * i) & 31]), a.scale_log2, neg_m));
+                    const float p1 = fast_exp2(fmaf(__uint_as_float(sv[i >> 4][(2 * i + 1) & 31]), a.scale_log2, neg_m));
+                    sum[i & 3] += p0 + p1;
+                    packed[i] = pack_bf16(p0, p1);
+                }
+                l_part = l_part * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
                 // PV of the previous tile must be done before O is rescaled; waiting for it here,
                 // before P(tt) is released, also keeps every o_done wait exactly one phase
                 // ahead (PV(tt) cannot start before this thread arrives on p_full below).
@@ -320,34 +344,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     const float f = rescale ? alpha : 1.0f;
 #pragma unroll 1
-                    for (int c = 0; c < 8; ++c) {
+                    for (int c = 0; c < 4; ++c) {
                         uint32_t o[32];
-                        tmem_ld32(lane_base + kColO + c * 32, o);
+                        const uint32_t oa = lane_base + kColO + half * 128 + c * 32;
+                        tmem_ld32(oa, o);
                         tc_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-                        tmem_st32(lane_base + kColO + c * 32, o);
+                        tmem_st32(oa, o);
                     }
                 }
-                // P (bf16 pairs) over the first 64 columns of this tile's S buffer
-                tmem_st32(s_addr, packed[0]);
-                tmem_st32(s_addr + 32, packed[1]);
+                // P (bf16 pairs): this half's 64 keys -> columns [32*half, 32*half + 32) of the S buffer
+                tmem_st32(lane_base + kColS + (tt & 1) * 128 + half * 32, packed);
                 tc_wait_st();
                 tc_fence_before();
                 mbar_arrive(bar(kBarP + (tt & 1)));
             }
             if (!alive) break;
-            // epilogue: O / l -> bf16 out[b][t][h][:]
+            // epilogue: O / l -> bf16 out[b][t][h][half*128 ...]
             wait_o(static_cast<int64_t>(gt + g.n_tiles) - 1);
-            if (!alive) break;
+            float l_other;
+            if (!exchange(l_part, l_other) || !alive) {
+                alive = false;
+                break;
+            }
             tc_fence_after();
+            const float l_run = l_part + l_other;
             const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
             const bool row_valid = r < g.rows_valid;
-            uint16_t *orow = a.out + ((static_cast<uint64_t>(g.b) * a.T + t) * a.q_heads + g.h) * kD;
+            uint16_t *orow = a.out + ((static_cast<uint64_t>(g.b) * a.T + t) * a.q_heads + g.h) * kD + half * 128;
 #pragma unroll 1
-            for (int c = 0; c < 8; ++c) {
+            for (int c = 0; c < 4; ++c) {
                 uint32_t o[32];
-                tmem_ld32(lane_base + kColO + c * 32, o);
+                tmem_ld32(lane_base + kColO + half * 128 + c * 32, o);
                 tc_wait_ld();
                 if (row_valid) {
                     uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 32);
@@ -445,27 +474,47 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
             if (i < a.rope_pairs) sincos_angle(pos * a.rope.inv_freq[i], sn[e], cs[e]);
             else cs[e] = 1.f, sn[e] = 0.f;
         }
-        // q rows -> workspace (head-major)
+        // q rows -> workspace (head-major); 8 rows per batch, all 8 loads in flight together
         const uint16_t *qsrc = a.q_raw + bt * a.q_heads * kD;
-        for (uint32_t h = 0; h < a.q_heads; ++h) {
-            float x[8];
-            unpack8(*reinterpret_cast<const uint4 *>(qsrc + h * kD + 8 * lane), x);
-            norm_rope_cs(x, lane, a.qk_norm, qw, a.eps, a.rope_pairs != 0, a.rope_pairs, cs, sn);
-            uint16_t *dst = a.q_ws + ((static_cast<uint64_t>(b) * a.q_heads + h) * a.T + t) * kD;
-            *reinterpret_cast<uint4 *>(dst + 8 * lane) = pack8(x);
+        for (uint32_t h0 = 0; h0 < a.q_heads; h0 += 8) {
+            uint4 raw[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (h0 + u < a.q_heads) raw[u] = *reinterpret_cast<const uint4 *>(qsrc + (h0 + u) * kD + 8 * lane);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (h0 + u >= a.q_heads) break;
+                float x[8];
+                unpack8(raw[u], x);
+                norm_rope_cs(x, lane, a.qk_norm, qw, a.eps, a.rope_pairs != 0, a.rope_pairs, cs, sn);
+                uint16_t *dst = a.q_ws + ((static_cast<uint64_t>(b) * a.q_heads + h0 + u) * a.T + t) * kD;
+                *reinterpret_cast<uint4 *>(dst + 8 * lane) = pack8(x);
+            }
         }
-        // k and v rows -> caches at position pos0 + t
+        // k and v rows -> caches at position pos0 + t; 4 heads of each per batch
         const uint16_t *ksrc = a.k_raw + bt * a.kv_heads * kD;
         const uint16_t *vsrc = a.v_raw + bt * a.kv_heads * kD;
-        for (uint32_t h = 0; h < a.kv_heads; ++h) {
-            const uint64_t off = ((static_cast<uint64_t>(b) * a.kv_heads + h) * a.capacity + a.pos0 + t) * kD;
-            float x[8], y[8];
-            unpack8(*reinterpret_cast<const uint4 *>(ksrc + h * kD + 8 * lane), x);
-            unpack8(*reinterpret_cast<const uint4 *>(vsrc + h * kD + 8 * lane), y);
-            norm_rope_cs(x, lane, a.qk_norm, kw, a.eps, a.rope_pairs != 0, a.rope_pairs, cs, sn);
-            norm_rope_cs(y, lane, a.v_norm, ones, a.eps, false, 0, cs, sn);
-            *reinterpret_cast<uint4 *>(a.k_cache + off + 8 * lane) = pack8(x);
-            *reinterpret_cast<uint4 *>(a.v_cache + off + 8 * lane) = pack8(y);
+        for (uint32_t h0 = 0; h0 < a.kv_heads; h0 += 4) {
+            uint4 kr[4], vr[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (h0 + u < a.kv_heads) {
+                    kr[u] = *reinterpret_cast<const uint4 *>(ksrc + (h0 + u) * kD + 8 * lane);
+                    vr[u] = *reinterpret_cast<const uint4 *>(vsrc + (h0 + u) * kD + 8 * lane);
+                }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (h0 + u >= a.kv_heads) break;
+                const uint64_t off =
+                    ((static_cast<uint64_t>(b) * a.kv_heads + h0 + u) * a.capacity + a.pos0 + t) * kD;
+                float x[8], y[8];
+                unpack8(kr[u], x);
+                unpack8(vr[u], y);
+                norm_rope_cs(x, lane, a.qk_norm, kw, a.eps, a.rope_pairs != 0, a.rope_pairs, cs, sn);
+                norm_rope_cs(y, lane, a.v_norm, ones, a.eps, false, 0, cs, sn);
+                *reinterpret_cast<uint4 *>(a.k_cache + off + 8 * lane) = pack8(x);
+                *reinterpret_cast<uint4 *>(a.v_cache + off + 8 * lane) = pack8(y);
+            }
         }
     }
 }
