@@ -47,7 +47,7 @@ constexpr uint32_t kSlotChunk = kBN * 128;           // 64 dims x 64 keys, 128 B
 constexpr uint32_t kSlotBytes = kBN * kD * 2;        // 32768
 constexpr uint32_t kOffSlots = 0;
 constexpr uint32_t kOffBar = kOffSlots + kSlots * kSlotBytes;
-constexpr uint32_t kNumBars = 32;
+constexpr uint32_t kNumBars = 40;
 constexpr uint32_t kOffItems = kOffBar + 8 * kNumBars;
 constexpr uint32_t kItemRing = 8;
 constexpr uint32_t kOffRed = kOffItems + 4 * kItemRing;  // float [2 parity][2 half][128]
@@ -63,7 +63,7 @@ static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // barrier indices (8 bytes each at kOffBar)
 constexpr int kBarQFull = 0, kBarQEmpty = 1, kBarFull = 2, kBarEmpty = kBarFull + kSlots,
-              kBarS = kBarEmpty + kSlots, kBarP = kBarS + 2, kBarO = kBarP + 2, kBarOFree = kBarO + 1,
+              kBarS = kBarEmpty + kSlots, kBarP = kBarS + 2, kBarO = kBarP + 2, kBarOFree = kBarO + 2,
               kBarItem = kBarOFree + 1, kBarRed = kBarItem + kItemRing;
 static_assert(kBarRed + 2 <= kNumBars, "barrier budget");
 
@@ -126,7 +126,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(bar(kBarP + i), 2 * kBM);
             mbar_init(bar(kBarRed + i), 2 * kBM);
         }
-        mbar_init(bar(kBarO), 1);
+        mbar_init(bar(kBarO + 0), 1);
+        mbar_init(bar(kBarO + 1), 1);
         mbar_init(bar(kBarOFree), 2 * kBM);
         for (uint32_t i = 0; i < kItemRing; ++i) mbar_init(bar(kBarItem + i), 1);
         fence_mbar_init();
@@ -197,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         smem_desc_sw128(sb + kOffSlots + vslot * kSlotBytes + ks * 2048, kSlotChunk, 1024);
                     tc_mma_ts(tmem + kColO, p_col + ks * 8, bd, idPV, (!first || ks > 0) ? 1u : 0u);
                 }
-                tc_commit(bar(kBarO));
+                tc_commit(bar(kBarO + (t & 1)));
                 tc_commit(bar(kBarEmpty + vslot));
             };
             for (uint32_t it = 0; alive; ++it) {
@@ -240,11 +241,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t r = quad * 32 + lane;                  // query row == TMEM lane
         const uint32_t lane_base = tmem + ((32u * quad) << 16);
         float *red = reinterpret_cast<float *>(base + kOffRed);  // [2 parity][2 half][128]
-        uint32_t gt = 0, o_seen = 0, xchg = 0;
+        uint32_t gt = 0, xchg = 0;
         bool alive = true;
-        auto wait_o = [&](int64_t upto) {
-            while (alive && static_cast<int64_t>(o_seen) <= upto)
-                alive = __all_sync(0xffffffffu, mbar_wait(bar(kBarO), o_seen++ & 1, a.status));
+        // Wait for PV of global tile t.  o_done is a ring of two barriers indexed by tile parity:
+        // when this runs (after S(t+1) or S(t) completed), PV(t-2) is already complete (it was
+        // issued before those S MMAs) and PV(t+2) cannot have started, so the parity is
+        // unambiguous without observing every phase.
+        auto wait_pv = [&](uint32_t t) {
+            alive = alive && __all_sync(0xffffffffu, mbar_wait(bar(kBarO + (t & 1)), (t >> 1) & 1, a.status));
         };
         // The handshake also orders TMEM: each half has finished reading its S columns before it
         // arrives, and half 1 overwrites some of half 0's S columns with P only after the wait.
@@ -351,13 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     packed[i] = pack_bf16(p0, p1);
                 }
                 l_part = l_part * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
-                // PV of the previous tile must be done before O is rescaled; waiting for it here,
-                // before P(tt) is released, also keeps every o_done wait exactly one phase
-                // ahead (PV(tt) cannot start before this thread arrives on p_full below).
-                wait_o(static_cast<int64_t>(tt) - 1);
-                if (!alive) break;
-                // tcgen05.ld/st are warp-collective: the whole warp rescales if any row must.
+                // tcgen05.ld/st are warp-collective: the whole warp rescales if any row must, after
+                // PV of the previous tile has finished accumulating into O.
                 if (__any_sync(0xffffffffu, rescale)) {
+                    wait_pv(tt - 1);
+                    if (!alive) break;
                     tc_fence_after();
                     const float f = rescale ? alpha : 1.0f;
 #pragma unroll 1
@@ -393,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!alive) break;
             }
             // epilogue: O / l -> bf16 out[b][t][h][half*128 ...]
-            wait_o(static_cast<int64_t>(gt + cur_n) - 1);
+            wait_pv(gt + cur_n - 1);
             float l_other;
             if (!exchange(l_part, l_other) || !alive) {
                 alive = false;
