@@ -7,29 +7,33 @@
 // o = softmax(scale * q K^T) V over keys p - window < j <= p (or j <= p), GQA map h/(Hq/Hkv).
 //
 // Two launches per call:
-//  1. prep: one warp per (sequence, token): the token's RoPE cos/sin are computed once and
-//     reused for its Hq + Hkv rows; every row is one 16-byte load and store per lane.  q goes
-//     to a head-major workspace [B][Hq][T][256] (one 3-D TMA box per 128-query tile), k and v
-//     to the caches.  It also zeroes the attention kernel's scheduler counters.
-//  2. attention: a persistent kernel, one CTA per SM, pulling work items (128-query tile x q
-//     head) from an atomic counter, heaviest tiles first (items are ordered by query tile,
-//     last first).  Per CTA, 12 warps:
-//       warp 0  scheduler + TMA producer: K and V as 64-key tiles (32 KB each) through a
-//               7-slot ring; 3-D tensor maps end at pos0+T, so keys past the valid cache read
-//               as zeros, never as uninitialised memory.
-//       warp 1  TMEM owner (512 columns) and tcgen05.mma issuer (one thread), both products in
-//               the A-from-TMEM form of .kind::f16, so shared memory only feeds B:
-//               S_t = Q K_t^T (M=128, N=64, K=16 x 16), Q in TMEM, K K-major in smem;
-//               O += P_t V_t  (M=128, N=256, K=16 x 4), P in TMEM, V MN-major in smem.
-//               S_{t+1} is issued before PV_t, and the next item's S MMAs run while the
-//               current item's epilogue drains O.
+//  1. prep: one warp per (sequence, token, head group): the token's RoPE cos/sin are computed
+//     once and reused for its rows; every row is one 16-byte load and store per lane.  q goes to
+//     a head-major workspace [B][Hq][T][256] (one 3-D TMA box per 128-query tile), k and v to
+//     the caches.  It also zeroes the attention kernel's scheduler counters.
+//  2. attention: a persistent kernel of CTA pairs (clusters of two on two SMs).  A pair takes
+//     work items from an atomic counter, heaviest first: 256 query rows = the same 128 queries
+//     for the two q heads of a GQA group (head 2i+r in CTA r) when the group size is even,
+//     else 256 consecutive queries of one head (rows 128r.. in CTA r).  Both products are
+//     M=256 tcgen05.mma.cta_group::2.kind::f16 issued by one thread of CTA 0:
+//       S_t = Q K_t^T  (N=128 keys, K=256): Q (128 rows x 256, this CTA's) and this CTA's half
+//                      of the key tile (64 keys x 256) in shared memory, K-major;
+//       O += P_t V_t   (N=256 dims, K=128 keys): P in TMEM, this CTA's half of V (128 keys x
+//                      128 dims) in shared memory, MN-major.
+//     so each SM streams half of every K/V tile that serves 256 query rows.  Per CTA, 12 warps:
+//       warp 0  TMA producer (CTA 0's also takes items and sends them to CTA 1): 16 KB ring
+//               slots in consumption order K(0) K(1) V(0) K(2) V(1) ...; all copies of the pair
+//               complete on CTA 0's barriers; tensor maps end at pos0+T (keys past the valid
+//               cache read as zeros).
+//       warp 1  TMEM owner (512 columns, allocated for the pair); in CTA 0, the MMA issuer.
+//               S_{t+1} is issued before PV_t.
 //       warps 4-11  two warpgroups per 128 query rows (TMEM lane = row; half 0 takes keys
-//               0-31 of each tile and dims 0-127, half 1 keys 32-63 and dims 128-255): they put
-//               each item's normalised q into TMEM, run the online softmax (log2 domain, mask
-//               only on tiles crossing the causal/window band, lazy rescaling of O when a row
-//               max grows by more than 2^8, row max and sum exchanged between the halves), store
-//               P as bf16 pairs over their S columns, and write the epilogue.
-//     TMEM: O = columns [0, 256), Q = [256, 384), S0/P0 = [384, 448), S1/P1 = [448, 512).
+//               0-63 of each tile and dims 0-127, half 1 keys 64-127 and dims 128-255): online
+//               softmax in the log2 domain (mask only on tiles crossing the causal/window
+//               band; O rescaled in TMEM only when a row max grows by more than 2^8; row max
+//               and sum exchanged between the halves), P as bf16 pairs over the first 32 of the
+//               half's own S columns, and the epilogue.
+//     TMEM (each CTA, its 128 rows): O = columns [0, 256), S0/P0 = [256, 384), S1/P1 = [384, 512).
 #include <algorithm>
 
 #include "common.cuh"
@@ -40,28 +44,33 @@ namespace apex {
 namespace {
 
 constexpr int kD = 256;
-constexpr int kBM = 128;                             // queries per item
-constexpr int kBN = 64;                              // keys per tile (one ring slot of K, one of V)
-constexpr int kSlots = 7;
-constexpr uint32_t kSlotChunk = kBN * 128;           // 64 dims x 64 keys, 128 B per key row
-constexpr uint32_t kSlotBytes = kBN * kD * 2;        // 32768
-constexpr uint32_t kOffSlots = 0;
+constexpr int kBM = 128;                             // query rows per CTA
+constexpr int kBN = 128;                             // keys per tile (both CTAs)
+constexpr int kSlots = 10;
+constexpr uint32_t kChunk = 64 * 128;                // 64 rows x 128 B (one TMA box)
+constexpr uint32_t kSlotBytes = 2 * kChunk;          // 16 KB
+constexpr uint32_t kQBytes = kBM * kD * 2;           // 64 KB
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffSlots = kQBytes;
 constexpr uint32_t kOffBar = kOffSlots + kSlots * kSlotBytes;
 constexpr uint32_t kNumBars = 40;
 constexpr uint32_t kOffItems = kOffBar + 8 * kNumBars;
 constexpr uint32_t kItemRing = 8;
 constexpr uint32_t kOffRed = kOffItems + 4 * kItemRing;  // float [2 parity][2 half][128]
-constexpr uint32_t kOffTmem = kOffRed + 2 * 2 * 128 * 4;
+constexpr uint32_t kOffFlag = kOffRed + 2 * 2 * 128 * 4;
+constexpr uint32_t kOffTmem = kOffFlag + 16;
 constexpr uint32_t kSmemBytes = kOffTmem + 16;  // the dynamic shared memory base is 1024-aligned
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 0, kColQ = 256, kColS = 384;  // O f32 [0,256), Q bf16 pairs [256,384), S 2 x 64
-constexpr int kThreads = 384;                        // 12 warps: 0 TMA, 1 MMA, 4-11 softmax
+constexpr uint32_t kColO = 0, kColS = 256;
+constexpr int kThreads = 384;                        // 12 warps: 0 TMA, 1 TMEM/MMA, 4-11 softmax
 constexpr float kTau = 8.0f;                         // lazy-rescale threshold (log2 units)
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint32_t kPairWarps = 16;                  // softmax warps of both CTAs
 
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-// barrier indices (8 bytes each at kOffBar)
+// barrier indices (8 bytes each at kOffBar).  CTA 0's copies of QFull, Full, P and OFree count
+// the pair; Empty, QEmpty, S and O are signalled in both CTAs by multicast commits.
 constexpr int kBarQFull = 0, kBarQEmpty = 1, kBarFull = 2, kBarEmpty = kBarFull + kSlots,
               kBarS = kBarEmpty + kSlots, kBarP = kBarS + 2, kBarO = kBarP + 2, kBarOFree = kBarO + 2,
               kBarItem = kBarOFree + 1, kBarRed = kBarItem + kItemRing;
@@ -69,266 +78,325 @@ static_assert(kBarRed + 2 <= kNumBars, "barrier budget");
 
 struct PrefillArgs {
     uint16_t *out;        // [B][T][Hq][D]
-    const uint16_t *q;    // normalised q [B][Hq][T][D] (the workspace)
     unsigned *status;     // device status word
     unsigned *sched;      // [0] next item, [1] CTAs done (zeroed by the prep kernel)
-    uint32_t batch, T, pos0, q_heads, kv_heads, window, n_qtiles, n_items;
+    uint32_t batch, T, pos0, kv_len, q_heads, kv_heads, window, n_qtiles, n_items, pair_heads;
     float scale_log2;
 };
 
 struct Item {
-    uint32_t b, h, kvh, t0, rows_valid, pos_first, pos_last, j_start, n_tiles;
+    uint32_t b, h, kvh, t0, rows_valid, q_row;  // this CTA's head, first query, valid rows, q box row
+    uint32_t pos_first, pos_last;               // positions of this CTA's rows
+    uint32_t j_start, n_tiles;                  // key tiles of the pair
 };
 
-__device__ __forceinline__ Item item_geometry(uint32_t idx, const PrefillArgs &a) {
+__device__ __forceinline__ Item item_geometry(uint32_t idx, const PrefillArgs &a, uint32_t rank) {
     Item it;
-    const uint32_t bh_count = a.batch * a.q_heads;
-    const uint32_t qt = a.n_qtiles - 1 - idx / bh_count;  // last query tiles (most keys) first
-    const uint32_t bh = idx % bh_count;
-    it.b = bh / a.q_heads;
-    it.h = bh % a.q_heads;
+    uint32_t t0_pair, span;
+    if (a.pair_heads) {  // two heads of one GQA group, same 128 queries
+        const uint32_t pairs = a.q_heads / 2, per_tile = a.batch * pairs;
+        const uint32_t qt = a.n_qtiles - 1 - idx / per_tile;  // last query tiles (most keys) first
+        const uint32_t bp = idx % per_tile;
+        it.b = bp / pairs;
+        it.h = 2 * (bp % pairs) + rank;
+        t0_pair = qt * kBM;
+        it.t0 = t0_pair;
+        span = kBM;
+    } else {  // one head, 256 consecutive queries
+        const uint32_t per_tile = a.batch * a.q_heads;
+        const uint32_t qt = a.n_qtiles - 1 - idx / per_tile;
+        const uint32_t bh = idx % per_tile;
+        it.b = bh / a.q_heads;
+        it.h = bh % a.q_heads;
+        t0_pair = qt * 2 * kBM;
+        it.t0 = t0_pair + rank * kBM;
+        span = 2 * kBM;
+    }
     it.kvh = it.h / (a.q_heads / a.kv_heads);
-    it.t0 = qt * kBM;
-    it.rows_valid = min(static_cast<uint32_t>(kBM), a.T - it.t0);
+    it.rows_valid = a.T > it.t0 ? min(static_cast<uint32_t>(kBM), a.T - it.t0) : 0u;
+    it.q_row = min(it.t0, a.T - 1);  // a q box always starts inside the workspace
     it.pos_first = a.pos0 + it.t0;
-    it.pos_last = it.pos_first + it.rows_valid - 1;
-    const uint32_t kv_lo = (a.window && it.pos_first + 1 > a.window) ? it.pos_first + 1 - a.window : 0;
+    it.pos_last = it.pos_first + (it.rows_valid ? it.rows_valid - 1 : 0u);
+    const uint32_t pair_first = a.pos0 + t0_pair;
+    const uint32_t pair_last = a.pos0 + min(a.T, t0_pair + span) - 1;
+    const uint32_t kv_lo = (a.window && pair_first + 1 > a.window) ? pair_first + 1 - a.window : 0;
     it.j_start = (kv_lo / kBN) * kBN;
-    it.n_tiles = (it.pos_last - it.j_start) / kBN + 1;
+    it.n_tiles = (pair_last - it.j_start) / kBN + 1;
     return it;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-    prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                      const PrefillArgs a) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *base = smem_raw;
     const uint32_t sb = smem_u32(base);
-    if (sb & 1023u) {  // the swizzled tiles need 1024-byte alignment; never expected to fire
+    if (sb & 1023u) {  // same layout in both CTAs: both leave before any pair operation
         if (threadIdx.x == 0) atomicOr(a.status, kStatusTimeout);
         return;
     }
     auto bar = [&](int i) { return sb + kOffBar + 8u * i; };
     volatile int *items = reinterpret_cast<volatile int *>(base + kOffItems);
+    volatile uint32_t *err_flag = reinterpret_cast<volatile uint32_t *>(base + kOffFlag);
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(base + kOffTmem);
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
 
     if (tid == 0) {
-        mbar_init(bar(kBarQFull), 2 * kBM);   // Q in TMEM, written by the softmax threads
-        mbar_init(bar(kBarQEmpty), 1);        // the item's last S MMA done with Q
+        mbar_init(bar(kBarQFull), 1);
+        mbar_init(bar(kBarQEmpty), 1);
         for (int i = 0; i < kSlots; ++i) {
             mbar_init(bar(kBarFull + i), 1);
             mbar_init(bar(kBarEmpty + i), 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar(kBarS + i), 1);
-            mbar_init(bar(kBarP + i), 2 * kBM);
+            mbar_init(bar(kBarP + i), kPairWarps);
+            mbar_init(bar(kBarO + i), 1);
             mbar_init(bar(kBarRed + i), 2 * kBM);
         }
-        mbar_init(bar(kBarO + 0), 1);
-        mbar_init(bar(kBarO + 1), 1);
-        mbar_init(bar(kBarOFree), 2 * kBM);
+        mbar_init(bar(kBarOFree), kPairWarps);
         for (uint32_t i = 0; i < kItemRing; ++i) mbar_init(bar(kBarItem + i), 1);
+        *err_flag = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_holder), kTmemCols);
-        tmem_relinquish();
+        tmem_alloc_pair(smem_u32(tmem_holder), kTmemCols);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    bool alive = true;
 
     if (warp == 0) {
-        // ------------------------------------------------------------ scheduler + TMA producer
+        // ------------------------------------------------------------ TMA producer (+ scheduler in CTA 0)
         if (lane == 0) {
+            prefetch_tensormap(&tm_q);
             prefetch_tensormap(&tm_k);
             prefetch_tensormap(&tm_v);
-            uint32_t kv_n = 0;
-            bool alive = true;
+            uint32_t n = 0;  // ring position (same sequence in both CTAs and the MMA issuer)
+            auto next_slot = [&](uint32_t &dst, uint32_t &full) {
+                const uint32_t slot = n % kSlots;
+                if (n >= kSlots && !mbar_wait_cluster(bar(kBarEmpty + slot), ((n / kSlots) - 1) & 1, a.status))
+                    return false;
+                if (leader) mbar_arrive_expect_tx(bar(kBarFull + slot), 2 * kSlotBytes);
+                dst = sb + kOffSlots + slot * kSlotBytes;
+                full = mapa(bar(kBarFull + slot), 0);
+                ++n;
+                return true;
+            };
             for (uint32_t it = 0;; ++it) {
-                int idx = static_cast<int>(atomicAdd(a.sched, 1u));
-                if (static_cast<uint32_t>(idx) >= a.n_items || !alive) idx = -1;
-                items[it % kItemRing] = idx;
-                mbar_arrive(bar(kBarItem + it % kItemRing));
+                const uint32_t is = it % kItemRing;
+                int idx;
+                if (leader) {
+                    const uint32_t claimed = alive ? atomicAdd(a.sched, 1u) : a.n_items;
+                    idx = claimed < a.n_items ? static_cast<int>(claimed) : -1;
+                    items[is] = idx;
+                    st_cluster_u32(mapa(sb + kOffItems + 4 * is, 1), static_cast<uint32_t>(idx));
+                    mbar_arrive(bar(kBarItem + is));
+                    mbar_arrive_cluster(mapa(bar(kBarItem + is), 1));
+                } else {
+                    if (!mbar_wait_cluster(bar(kBarItem + is), (it / kItemRing) & 1, a.status)) {
+                        alive = false;
+                        break;
+                    }
+                    idx = items[is];
+                }
                 if (idx < 0) break;
-                const Item g = item_geometry(static_cast<uint32_t>(idx), a);
-                for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
-                    const uint32_t key0 = g.j_start + j * kBN;
-                    for (int which = 0; which < 2; ++which, ++kv_n) {  // K then V
-                        const uint32_t slot = kv_n % kSlots;
-                        if (kv_n >= kSlots &&
-                            !mbar_wait(bar(kBarEmpty + slot), ((kv_n / kSlots) - 1) & 1, a.status)) {
-                            alive = false;
-                            break;
+                const Item g = item_geometry(static_cast<uint32_t>(idx), a, rank);
+                const int32_t kv_row = static_cast<int32_t>(g.b * a.kv_heads + g.kvh);
+                // a box never starts past the cache end; the keys it then holds are masked
+                auto key_row = [&](uint32_t key) { return static_cast<int32_t>(min(key, a.kv_len - 1)); };
+                for (uint32_t j = 0; j <= g.n_tiles && alive; ++j) {
+                    if (j < g.n_tiles) {  // K(j): this CTA's 64 keys, dims [0,128) then [128,256)
+                        const uint32_t key = g.j_start + j * kBN + 64 * rank;
+                        for (int s = 0; s < 2 && alive; ++s) {
+                            uint32_t dst, full;
+                            if (!next_slot(dst, full)) {
+                                alive = false;
+                                break;
+                            }
+                            for (int c = 0; c < 2; ++c)
+                                tma_load_3d_pair(dst + c * kChunk, &tm_k, 128 * s + 64 * c, key_row(key), kv_row, full);
                         }
-                        mbar_arrive_expect_tx(bar(kBarFull + slot), kSlotBytes);
-                        const uint32_t dst = sb + kOffSlots + slot * kSlotBytes;
-                        const CUtensorMap *map = which == 0 ? &tm_k : &tm_v;
-                        for (int c = 0; c < 4; ++c)
-                            tma_load_3d(dst + c * kSlotChunk, map, c * 64, static_cast<int32_t>(key0),
-                                        static_cast<int32_t>(g.b * a.kv_heads + g.kvh), bar(kBarFull + slot));
+                        if (j == 0 && alive) {  // Q, once the previous item's S MMAs are done with it
+                            if (it >= 1 && !mbar_wait_cluster(bar(kBarQEmpty), (it - 1) & 1, a.status)) {
+                                alive = false;
+                                break;
+                            }
+                            if (leader) mbar_arrive_expect_tx(bar(kBarQFull), 2 * kQBytes);
+                            const uint32_t full = mapa(bar(kBarQFull), 0);
+                            for (int c = 0; c < 4; ++c)
+                                tma_load_3d_pair(sb + kOffQ + c * (kQBytes / 4), &tm_q, 64 * c,
+                                                 static_cast<int32_t>(g.q_row),
+                                                 static_cast<int32_t>(g.b * a.q_heads + g.h), full);
+                        }
+                    }
+                    if (j >= 1) {  // V(j-1): this CTA's 128 dims, keys [0,64) then [64,128)
+                        const uint32_t key = g.j_start + (j - 1) * kBN;
+                        for (int s = 0; s < 2 && alive; ++s) {
+                            uint32_t dst, full;
+                            if (!next_slot(dst, full)) {
+                                alive = false;
+                                break;
+                            }
+                            for (int c = 0; c < 2; ++c)
+                                tma_load_3d_pair(dst + c * kChunk, &tm_v, 128 * rank + 64 * c, key_row(key + 64 * s),
+                                                 kv_row, full);
+                        }
                     }
                 }
             }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idS = idesc_bf16_f32(kBM, kBN, 0, 0);
-            constexpr uint32_t idPV = idesc_bf16_f32(kBM, kD, 0, 1);
-            uint32_t gt = 0, kv_n = 0;
-            bool alive = true;
-            auto wait_full = [&](uint32_t n) { return mbar_wait(bar(kBarFull + n % kSlots), (n / kSlots) & 1, a.status); };
-            // O += P_t V_t for global tile t; V at ring position nv; P in TMEM over S buffer t%2
-            auto issue_pv = [&](uint32_t t, uint32_t nv, bool first, uint32_t it) {
+        // ------------------------------------------------------------ MMA issuer (CTA 0)
+        if (leader && lane == 0) {
+            constexpr uint32_t idS = idesc_bf16_f32(2 * kBM, kBN, 0, 0);
+            constexpr uint32_t idPV = idesc_bf16_f32(2 * kBM, kD, 0, 1);
+            uint32_t gt = 0, n = 0;
+            auto wait_full = [&](uint32_t m) {
+                return mbar_wait_cluster(bar(kBarFull + m % kSlots), (m / kSlots) & 1, a.status);
+            };
+            // O += P_t V_t; V(t) is the next two ring slots (keys [0,64) and [64,128)); P_t in TMEM
+            // over S buffer t%2: keys [0,64) in columns [0,32), keys [64,128) in [64,96).
+            auto issue_pv = [&](uint32_t t, bool first, uint32_t it) {
                 if (!alive) return;
-                alive = mbar_wait(bar(kBarP + (t & 1)), (t >> 1) & 1, a.status);
-                if (alive && first && it >= 1) alive = mbar_wait(bar(kBarOFree), (it - 1) & 1, a.status);
-                alive = alive && wait_full(nv);
+                alive = mbar_wait_cluster(bar(kBarP + (t & 1)), (t >> 1) & 1, a.status);
+                if (alive && first && it >= 1) alive = mbar_wait_cluster(bar(kBarOFree), (it - 1) & 1, a.status);
                 if (!alive) return;
                 tc_fence_after();
                 const uint32_t p_col = tmem + kColS + (t & 1) * kBN;
-                const uint32_t vslot = nv % kSlots;
+                for (int s = 0; s < 2; ++s) {
+                    if (!wait_full(n)) {
+                        alive = false;
+                        return;
+                    }
+                    tc_fence_after();
+                    const uint32_t slot = n % kSlots;
 #pragma unroll
-                for (int ks = 0; ks < kBN / 16; ++ks) {
-                    const uint64_t bd =
-                        smem_desc_sw128(sb + kOffSlots + vslot * kSlotBytes + ks * 2048, kSlotChunk, 1024);
-                    tc_mma_ts(tmem + kColO, p_col + ks * 8, bd, idPV, (!first || ks > 0) ? 1u : 0u);
+                    for (int ks = 0; ks < 4; ++ks) {
+                        const uint64_t bd =
+                            smem_desc_sw128(sb + kOffSlots + slot * kSlotBytes + ks * 2048, kChunk, 1024);
+                        tc_mma_ts_pair(tmem + kColO, p_col + s * 64 + ks * 8, bd, idPV,
+                                       (!first || s > 0 || ks > 0) ? 1u : 0u);
+                    }
+                    tc_commit_pair_both(bar(kBarEmpty + slot));
+                    ++n;
                 }
-                tc_commit(bar(kBarO + (t & 1)));
-                tc_commit(bar(kBarEmpty + vslot));
+                tc_commit_pair_both(bar(kBarO + (t & 1)));
             };
             for (uint32_t it = 0; alive; ++it) {
                 if (!mbar_wait(bar(kBarItem + it % kItemRing), (it / kItemRing) & 1, a.status)) break;
                 const int idx = items[it % kItemRing];
                 if (idx < 0) break;
-                if (!mbar_wait(bar(kBarQFull), it & 1, a.status)) break;  // Q of this item in TMEM
+                const Item g = item_geometry(static_cast<uint32_t>(idx), a, 0);
+                if (!mbar_wait_cluster(bar(kBarQFull), it & 1, a.status)) break;
                 tc_fence_after();
-                const Item g = item_geometry(static_cast<uint32_t>(idx), a);
                 for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
-                    const uint32_t t = gt + j, nk = kv_n + 2 * j;
-                    alive = wait_full(nk);
-                    if (!alive) break;
-                    tc_fence_after();
+                    const uint32_t t = gt + j;
                     const uint32_t s_col = tmem + kColS + (t & 1) * kBN;
-                    const uint32_t kslot = nk % kSlots;
+                    for (int s = 0; s < 2 && alive; ++s) {  // K(j) dims [128s, 128s+128)
+                        if (!wait_full(n)) {
+                            alive = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t slot = n % kSlots;
 #pragma unroll
-                    for (int ks = 0; ks < kD / 16; ++ks) {
-                        const uint64_t bd = smem_desc_sw128(
-                            sb + kOffSlots + kslot * kSlotBytes + (ks / 4) * kSlotChunk + (ks % 4) * 32, 16, 1024);
-                        tc_mma_ts(s_col, tmem + kColQ + ks * 8, bd, idS, ks > 0 ? 1u : 0u);
+                        for (int ks = 0; ks < 8; ++ks) {
+                            const int kk = 8 * s + ks;  // 16-dim step of the 256 dims
+                            const uint64_t ad = smem_desc_sw128(sb + kOffQ + (kk / 4) * (kQBytes / 4) + (kk % 4) * 32,
+                                                                16, 1024);
+                            const uint64_t bd = smem_desc_sw128(
+                                sb + kOffSlots + slot * kSlotBytes + (ks / 4) * kChunk + (ks % 4) * 32, 16, 1024);
+                            tc_mma_ss_pair(s_col, ad, bd, idS, kk > 0 ? 1u : 0u);
+                        }
+                        tc_commit_pair_both(bar(kBarEmpty + slot));
+                        ++n;
                     }
-                    tc_commit(bar(kBarS + (t & 1)));
-                    tc_commit(bar(kBarEmpty + kslot));
-                    if (j + 1 == g.n_tiles) tc_commit(bar(kBarQEmpty));  // Q is free once these finish
-                    if (j >= 1) issue_pv(t - 1, kv_n + 2 * (j - 1) + 1, j - 1 == 0, it);
+                    if (!alive) break;
+                    tc_commit_pair_both(bar(kBarS + (t & 1)));
+                    if (j + 1 == g.n_tiles) tc_commit_pair_both(bar(kBarQEmpty));  // Q free once these finish
+                    if (j >= 1) issue_pv(t - 1, j - 1 == 0, it);
                 }
-                issue_pv(gt + g.n_tiles - 1, kv_n + 2 * (g.n_tiles - 1) + 1, g.n_tiles == 1, it);
+                issue_pv(gt + g.n_tiles - 1, g.n_tiles == 1, it);
                 gt += g.n_tiles;
-                kv_n += 2 * g.n_tiles;
             }
         }
     } else if (warp >= 4) {
-        // ------------------------------------------------------------ Q loader, softmax, epilogue
-        // Two warpgroups share each query row: half 0 owns S columns [0, 32) of each 64-key tile,
-        // q/O dims [0, 128); half 1 owns S columns [32, 64), dims [128, 256).  The row max (every
-        // tile) and the row sum (every item) are exchanged through shared memory with an
-        // mbarrier handshake, so every wait stays bounded.
+        // ------------------------------------------------------------ softmax + epilogue (both CTAs)
         const uint32_t half = (warp - 4) >> 2, quad = warp & 3;
         const uint32_t r = quad * 32 + lane;                  // query row == TMEM lane
         const uint32_t lane_base = tmem + ((32u * quad) << 16);
+        const uint32_t p_bar0 = mapa(bar(kBarP), 0), p_bar1 = mapa(bar(kBarP + 1), 0);
+        const uint32_t ofree_bar = mapa(bar(kBarOFree), 0);
         float *red = reinterpret_cast<float *>(base + kOffRed);  // [2 parity][2 half][128]
         uint32_t gt = 0, xchg = 0;
-        bool alive = true;
         // Wait for PV of global tile t.  o_done is a ring of two barriers indexed by tile parity:
         // when this runs (after S(t+1) or S(t) completed), PV(t-2) is already complete (it was
         // issued before those S MMAs) and PV(t+2) cannot have started, so the parity is
         // unambiguous without observing every phase.
         auto wait_pv = [&](uint32_t t) {
-            alive = alive && __all_sync(0xffffffffu, mbar_wait(bar(kBarO + (t & 1)), (t >> 1) & 1, a.status));
+            alive = alive &&
+                    __all_sync(0xffffffffu, mbar_wait_cluster(bar(kBarO + (t & 1)), (t >> 1) & 1, a.status));
         };
-        // The handshake also orders TMEM: each half has finished reading its S columns before it
-        // arrives, and half 1 overwrites some of half 0's S columns with P only after the wait.
         auto exchange = [&](float mine, float &theirs) {
             const uint32_t slot = xchg & 1;
             red[(slot * 2 + half) * kBM + r] = mine;
-            tc_fence_before();
             mbar_arrive(bar(kBarRed + slot));
             const bool ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarRed + slot), (xchg >> 1) & 1, a.status));
-            tc_fence_after();
             theirs = red[(slot * 2 + (half ^ 1)) * kBM + r];
             ++xchg;
             return ok;
         };
-        // This row's q (this half's 128 dims) -> TMEM columns [kColQ + 64*half, +64) as bf16 pairs.
-        auto load_q = [&](const Item &g, uint32_t it) {
-            if (it >= 1 && !__all_sync(0xffffffffu, mbar_wait(bar(kBarQEmpty), (it - 1) & 1, a.status))) {
-                alive = false;
-                return;
-            }
-            const uint32_t t = g.t0 + r;
-            const uint16_t *src = a.q + ((static_cast<uint64_t>(g.b) * a.q_heads + g.h) * a.T + t) * kD + half * 128;
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t w[32];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const uint4 v = r < g.rows_valid ? *reinterpret_cast<const uint4 *>(src + c * 64 + u * 8)
-                                                     : make_uint4(0u, 0u, 0u, 0u);
-                    w[4 * u + 0] = v.x;
-                    w[4 * u + 1] = v.y;
-                    w[4 * u + 2] = v.z;
-                    w[4 * u + 3] = v.w;
-                }
-                tmem_st32(lane_base + kColQ + half * 64 + c * 32, w);
-            }
-            tc_wait_st();
+        // one elected lane per warp reports to CTA 0 after the warp's TMEM accesses are done
+        auto warp_arrive = [&](uint32_t cluster_bar) {
             tc_fence_before();
-            mbar_arrive(bar(kBarQFull));
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(cluster_bar);
         };
-        int idx = -1;
-        Item g{};
-        // item 0's q
-        if (__all_sync(0xffffffffu, mbar_wait(bar(kBarItem), 0, a.status))) {
-            idx = items[0];
-            if (idx >= 0) {
-                g = item_geometry(static_cast<uint32_t>(idx), a);
-                load_q(g, 0);
+        for (uint32_t it = 0; alive; ++it) {
+            if (!__all_sync(0xffffffffu, mbar_wait_cluster(bar(kBarItem + it % kItemRing), (it / kItemRing) & 1,
+                                                            a.status))) {
+                alive = false;
+                break;
             }
-        } else {
-            alive = false;
-        }
-        for (uint32_t it = 0; alive && idx >= 0; ++it) {
+            const int idx = items[it % kItemRing];
+            if (idx < 0) break;
+            const Item g = item_geometry(static_cast<uint32_t>(idx), a, rank);
             const uint32_t t = g.t0 + r;
             const int pos = static_cast<int>(a.pos0 + t);
             float m_run = -INFINITY, l_part = 0.f;
             for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
                 const uint32_t tt = gt + j;
-                bool ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarS + (tt & 1)), (tt >> 1) & 1, a.status));
+                bool ok = __all_sync(0xffffffffu,
+                                     mbar_wait_cluster(bar(kBarS + (tt & 1)), (tt >> 1) & 1, a.status));
                 tc_fence_after();
-                uint32_t sv[32];
-                const uint32_t s_addr = lane_base + kColS + (tt & 1) * kBN + half * 32;
+                uint32_t sv[64];
+                const uint32_t s_addr = lane_base + kColS + (tt & 1) * kBN + half * 64;
                 if (ok) {
-                    tmem_ld32(s_addr, sv);
+                    tmem_ld64(s_addr, sv);
                     tc_wait_ld();
                 }
                 const uint32_t tile0 = g.j_start + j * kBN;
-                const bool need_mask = (tile0 + kBN - 1 > g.pos_first) || (a.window && tile0 + a.window <= g.pos_last);
+                const bool need_mask = g.rows_valid && ((tile0 + kBN - 1 > g.pos_first) ||
+                                                        (a.window && tile0 + a.window <= g.pos_last));
                 if (need_mask) {
                     // visible keys of this row relative to this half's first key: [lo, hi]
-                    const int key0 = static_cast<int>(tile0 + half * 32);
+                    const int key0 = static_cast<int>(tile0 + half * 64);
                     const int hi = pos - key0;
                     const int lo = a.window ? pos + 1 - static_cast<int>(a.window) - key0 : -(1 << 30);
 #pragma unroll
-                    for (int k = 0; k < 32; ++k)
+                    for (int k = 0; k < 64; ++k)
                         if (k > hi || k < lo) sv[k] = 0xff800000u;  // -inf
                 }
                 float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                for (int k = 0; k < 32; ++k) mx[k & 3] = fmaxf(mx[k & 3], __uint_as_float(sv[k]));
+                for (int k = 0; k < 64; ++k) mx[k & 3] = fmaxf(mx[k & 3], __uint_as_float(sv[k]));
                 const float mine = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
                 float other;
                 ok = exchange(mine, other) && ok;
@@ -341,14 +409,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bool rescale = false;
                 if (mt > m_run + kTau) {
                     alpha = fast_exp2(m_run - mt);  // 0 when m_run = -inf
-                    rescale = j > 0;
+                    rescale = j > 0 && m_run != -INFINITY;  // O holds only zeros while m_run = -inf
                     m_run = mt;
                 }
                 const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
                 float sum[4] = {0.f, 0.f, 0.f, 0.f};
-                uint32_t packed[16];
+                uint32_t packed[32];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
+                for (int i = 0; i < 32; ++i) {
                     const float p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * i]), a.scale_log2, neg_m));
                     const float p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * i + 1]), a.scale_log2, neg_m));
                     sum[i & 3] += p0 + p1;
@@ -373,29 +441,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tmem_st32(oa, o);
                     }
                 }
-                // P (bf16 pairs): this half's 32 keys -> columns [16*half, 16*half + 16) of the S buffer
-                tmem_st16(lane_base + kColS + (tt & 1) * kBN + half * 16, packed);
+                tmem_st32(s_addr, packed);  // P over the first 32 of this half's own S columns
                 tc_wait_st();
-                tc_fence_before();
-                mbar_arrive(bar(kBarP + (tt & 1)));
+                warp_arrive((tt & 1) ? p_bar1 : p_bar0);
             }
             if (!alive) break;
-            // the next item's q goes into TMEM now, so its S MMAs overlap this epilogue
-            const Item cur = g;
-            const uint32_t cur_n = g.n_tiles;
-            if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarItem + (it + 1) % kItemRing), ((it + 1) / kItemRing) & 1,
-                                                   a.status))) {
-                alive = false;
-                break;
-            }
-            idx = items[(it + 1) % kItemRing];
-            if (idx >= 0) {
-                g = item_geometry(static_cast<uint32_t>(idx), a);
-                load_q(g, it + 1);
-                if (!alive) break;
-            }
             // epilogue: O / l -> bf16 out[b][t][h][half*128 ...]
-            wait_pv(gt + cur_n - 1);
+            wait_pv(gt + g.n_tiles - 1);
             float l_other;
             if (!exchange(l_part, l_other) || !alive) {
                 alive = false;
@@ -404,9 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const float l_run = l_part + l_other;
             const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
-            const bool row_valid = r < cur.rows_valid;
-            uint16_t *orow =
-                a.out + ((static_cast<uint64_t>(cur.b) * a.T + t) * a.q_heads + cur.h) * kD + half * 128;
+            const bool row_valid = r < g.rows_valid;
+            uint16_t *orow = a.out + ((static_cast<uint64_t>(g.b) * a.T + t) * a.q_heads + g.h) * kD + half * 128;
 #pragma unroll 1
             for (int c = 0; c < 4; ++c) {
                 uint32_t o[32];
@@ -425,16 +476,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            tc_fence_before();
-            mbar_arrive(bar(kBarOFree));
-            gt += cur_n;
+            warp_arrive(ofree_bar);
+            gt += g.n_tiles;
         }
     }
+    // Teardown.  After a failed wait, copies or MMAs of this pair may still be in flight: give them
+    // time to land (bounded) before the pair releases TMEM and shared memory.
+    if (!alive) *err_flag = 1u;
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();
+    if (tid == 0 && *err_flag) {
+        const long long start = clock64();
+        while (clock64() - start < 400000ll) __nanosleep(1000);
+    }
+    cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        tmem_dealloc_pair(tmem, kTmemCols);
     }
     if (tid == 0) {
         // the last CTA to finish resets the scheduler for the next launch
@@ -614,22 +673,55 @@ int launch_prep(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t
     return check_cuda(cudaGetLastError(), "prefill prep launch");
 }
 
+// Clusters of two that fit on the device at once with this kernel's shared memory (some GPCs
+// have an odd number of SMs); queried once per device.
+uint32_t max_active_pairs() {
+    static int cached[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && cached[dev]) return static_cast<uint32_t>(cached[dev]);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * static_cast<uint32_t>(sm_count() / 2), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, prefill_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();  // clear the query's error; fall back to one pair per two SMs
+        n = sm_count() / 2;
+    }
+    if (dev < 64) cached[dev] = n;
+    return static_cast<uint32_t>(n);
+}
+
 int launch_attend(const apex_attn_params *p, void *workspace, const uint16_t *k_cache, const uint16_t *v_cache,
                   uint32_t capacity, uint32_t batch, uint32_t tokens, uint32_t pos0, uint16_t *out,
                   cudaStream_t s) {
-    CUtensorMap tk, tv;
+    CUtensorMap tq, tk, tv;
     const uint64_t kv_len = static_cast<uint64_t>(pos0) + tokens;
-    int rc = make_tensor_map_bf16_3d(&tk, k_cache, kD, kv_len, static_cast<uint64_t>(batch) * p->kv_heads, kD * 2ull,
-                                     static_cast<uint64_t>(capacity) * kD * 2, 64, kBN);
+    const uint64_t kv_rows = static_cast<uint64_t>(batch) * p->kv_heads;
+    // normalised q [B*Hq][T][256]: one box = 128 queries x 64 dims
+    int rc = make_tensor_map_bf16_3d(&tq, workspace, kD, tokens, static_cast<uint64_t>(batch) * p->q_heads, kD * 2ull,
+                                     static_cast<uint64_t>(tokens) * kD * 2, 64, kBM);
     if (rc) return rc;
-    rc = make_tensor_map_bf16_3d(&tv, v_cache, kD, kv_len, static_cast<uint64_t>(batch) * p->kv_heads, kD * 2ull,
-                                 static_cast<uint64_t>(capacity) * kD * 2, 64, kBN);
+    // caches [B*Hkv][capacity][256] cut at pos0+T: one box = 64 keys x 64 dims
+    rc = make_tensor_map_bf16_3d(&tk, k_cache, kD, kv_len, kv_rows, kD * 2ull, static_cast<uint64_t>(capacity) * kD * 2,
+                                 64, 64);
+    if (rc) return rc;
+    rc = make_tensor_map_bf16_3d(&tv, v_cache, kD, kv_len, kv_rows, kD * 2ull, static_cast<uint64_t>(capacity) * kD * 2,
+                                 64, 64);
     if (rc) return rc;
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr_set[dev]) {
-        rc = check_cuda(cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        rc = check_cuda(cudaFuncSetAttribute(prefill_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(kSmemBytes)),
                         "prefill smem attribute");
         if (rc) return rc;
@@ -637,17 +729,22 @@ int launch_attend(const apex_attn_params *p, void *workspace, const uint16_t *k_
     }
     PrefillArgs fa{};
     fa.out = out;
-    fa.q = static_cast<const uint16_t *>(workspace);
     fa.status = device_status_ptr();
     if (!fa.status) return fail(APEX_ERR_CUDA, "prefill: device status word unavailable");
     fa.sched = sched_ptr(workspace, batch, tokens, p->q_heads);
-    fa.batch = batch; fa.T = tokens; fa.pos0 = pos0; fa.q_heads = p->q_heads; fa.kv_heads = p->kv_heads;
-    fa.window = p->window;
-    fa.n_qtiles = (tokens + kBM - 1) / kBM;
-    fa.n_items = batch * p->q_heads * fa.n_qtiles;
+    fa.batch = batch; fa.T = tokens; fa.pos0 = pos0; fa.kv_len = static_cast<uint32_t>(kv_len);
+    fa.q_heads = p->q_heads; fa.kv_heads = p->kv_heads; fa.window = p->window;
+    fa.pair_heads = (p->q_heads / p->kv_heads) % 2 == 0;
+    if (fa.pair_heads) {
+        fa.n_qtiles = (tokens + kBM - 1) / kBM;
+        fa.n_items = batch * (p->q_heads / 2) * fa.n_qtiles;
+    } else {
+        fa.n_qtiles = (tokens + 2 * kBM - 1) / (2 * kBM);
+        fa.n_items = batch * p->q_heads * fa.n_qtiles;
+    }
     fa.scale_log2 = p->scale * kLog2e;
-    const uint32_t grid = std::min<uint32_t>(fa.n_items, static_cast<uint32_t>(sm_count()));
-    prefill_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(tk, tv, fa);
+    const uint32_t pairs = std::min<uint32_t>(fa.n_items, max_active_pairs());
+    prefill_pair_kernel<<<2 * pairs, kThreads, kSmemBytes, s>>>(tq, tk, tv, fa);
     return check_cuda(cudaGetLastError(), "prefill attention launch");
 }
 

@@ -114,3 +114,18 @@ def test_batched_prefill_equals_per_sequence():
     for b in (0, 2):
         one, _ = run_prefill(cfg, [b], 1536, 768)
         np.testing.assert_array_equal(got[b], one[0])
+
+
+@pytest.mark.parametrize("q_heads,kv_heads,T,window", [(8, 8, 700, 0), (16, 4, 515, 300), (6, 2, 300, 0),
+                                                        (16, 8, 1, 0), (8, 8, 129, 64)])
+def test_prefill_gqa_group_sizes(q_heads, kv_heads, T, window):
+    """Even groups pair the two heads of a group in one CTA pair; odd groups (incl. MHA) pair
+    256 consecutive queries of one head."""
+    cfg = dataclasses.replace(CONFIGS["c2_prefill_window"], q_heads=q_heads, kv_heads=kv_heads, seq_len=T,
+                              chunk=T, window=window, seed=61 + q_heads + T)
+    got, _ = run_prefill(cfg, [0], T, T)
+    rng = np.random.default_rng(T)
+    rows = sorted(set(edge_rows(T, window, extra=(255, 256, 257, 383, 384))) |
+                  set(rng.choice(T, min(T, 64), replace=False).tolist()))
+    ref = oracle_prefill_rows(cfg, 0, T, rows)
+    assert_close(got[0, rows], ref, f"Hq={q_heads} Hkv={kv_heads} T={T} window={window}")
