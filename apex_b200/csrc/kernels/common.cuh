@@ -44,6 +44,13 @@ __device__ __forceinline__ void sincos_angle(float angle, float &s, float &c) {
     c = static_cast<float>(dc);
 }
 
+// max of three floats in one instruction (sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -223,9 +230,17 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
-// Arrive on an mbarrier given by its shared::cluster address (this CTA's or the peer's).
+// Arrive on an mbarrier given by its shared::cluster address (this CTA's or the peer's), with
+// release at cluster scope: the arriving thread's earlier shared-memory writes (e.g. with
+// st_cluster_u32) are visible to a waiter that acquires at cluster scope.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// Arrive on an mbarrier given by its shared::cluster address, release at CTA scope only: for
+// hand-offs whose data is tensor memory, ordered by tcgen05.wait + tcgen05.fence around the
+// barrier rather than by the memory model.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
     uint32_t ok;

@@ -30,9 +30,10 @@
 //       warps 4-11  two warpgroups per 128 query rows (TMEM lane = row; half 0 takes keys
 //               0-63 of each tile and dims 0-127, half 1 keys 64-127 and dims 128-255): online
 //               softmax in the log2 domain (mask only on tiles crossing the causal/window
-//               band; O rescaled in TMEM only when a row max grows by more than 2^8; row max
-//               and sum exchanged between the halves), P as bf16 pairs over the first 32 of the
-//               half's own S columns, and the epilogue.
+//               band; O rescaled in TMEM only when a row max grows by more than 2^8).  Each
+//               half reads all 128 scores of its row for the max, so both halves reach the same
+//               max with no exchange; the row sums meet once per item.  P goes as bf16 pairs over
+//               the first 32 of the half's own S columns; then the epilogue.
 //     TMEM (each CTA, its 128 rows): O = columns [0, 256), S0/P0 = [256, 384), S1/P1 = [384, 512).
 #include <algorithm>
 
@@ -53,7 +54,7 @@ constexpr uint32_t kQBytes = kBM * kD * 2;           // 64 KB
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffSlots = kQBytes;
 constexpr uint32_t kOffBar = kOffSlots + kSlots * kSlotBytes;
-constexpr uint32_t kNumBars = 40;
+constexpr uint32_t kNumBars = 48;
 constexpr uint32_t kOffItems = kOffBar + 8 * kNumBars;
 constexpr uint32_t kItemRing = 8;
 constexpr uint32_t kOffRed = kOffItems + 4 * kItemRing;  // float [2 parity][2 half][128]
@@ -66,13 +67,15 @@ constexpr int kThreads = 384;                        // 12 warps: 0 TMA, 1 TMEM/
 constexpr float kTau = 8.0f;                         // lazy-rescale threshold (log2 units)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kPairWarps = 16;                  // softmax warps of both CTAs
+constexpr uint32_t kHalfWarps = 8;                   // one softmax half of both CTAs
 
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // barrier indices (8 bytes each at kOffBar).  CTA 0's copies of QFull, Full, P and OFree count
-// the pair; Empty, QEmpty, S and O are signalled in both CTAs by multicast commits.
+// the pair; Empty, QEmpty, S and O are signalled in both CTAs by multicast commits.  P is one
+// barrier per (softmax half, tile parity), so PV can start on the first 64 keys early.
 constexpr int kBarQFull = 0, kBarQEmpty = 1, kBarFull = 2, kBarEmpty = kBarFull + kSlots,
-              kBarS = kBarEmpty + kSlots, kBarP = kBarS + 2, kBarO = kBarP + 2, kBarOFree = kBarO + 2,
+              kBarS = kBarEmpty + kSlots, kBarP = kBarS + 2, kBarO = kBarP + 4, kBarOFree = kBarO + 2,
               kBarItem = kBarOFree + 1, kBarRed = kBarItem + kItemRing;
 static_assert(kBarRed + 2 <= kNumBars, "barrier budget");
 
@@ -151,9 +154,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_init(bar(kBarFull + i), 1);
             mbar_init(bar(kBarEmpty + i), 1);
         }
+        for (int i = 0; i < 4; ++i) mbar_init(bar(kBarP + i), kHalfWarps);
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar(kBarS + i), 1);
-            mbar_init(bar(kBarP + i), kPairWarps);
             mbar_init(bar(kBarO + i), 1);
             mbar_init(bar(kBarRed + i), 2 * kBM);
         }
@@ -181,7 +184,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t n = 0;  // ring position (same sequence in both CTAs and the MMA issuer)
             auto next_slot = [&](uint32_t &dst, uint32_t &full) {
                 const uint32_t slot = n % kSlots;
-                if (n >= kSlots && !mbar_wait_cluster(bar(kBarEmpty + slot), ((n / kSlots) - 1) & 1, a.status))
+                if (n >= kSlots && !mbar_wait(bar(kBarEmpty + slot), ((n / kSlots) - 1) & 1, a.status))
                     return false;
                 if (leader) mbar_arrive_expect_tx(bar(kBarFull + slot), 2 * kSlotBytes);
                 dst = sb + kOffSlots + slot * kSlotBytes;
@@ -224,7 +227,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 tma_load_3d_pair(dst + c * kChunk, &tm_k, 128 * s + 64 * c, key_row(key), kv_row, full);
                         }
                         if (j == 0 && alive) {  // Q, once the previous item's S MMAs are done with it
-                            if (it >= 1 && !mbar_wait_cluster(bar(kBarQEmpty), (it - 1) & 1, a.status)) {
+                            if (it >= 1 && !mbar_wait(bar(kBarQEmpty), (it - 1) & 1, a.status)) {
                                 alive = false;
                                 break;
                             }
@@ -259,18 +262,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             constexpr uint32_t idPV = idesc_bf16_f32(2 * kBM, kD, 0, 1);
             uint32_t gt = 0, n = 0;
             auto wait_full = [&](uint32_t m) {
-                return mbar_wait_cluster(bar(kBarFull + m % kSlots), (m / kSlots) & 1, a.status);
+                return mbar_wait(bar(kBarFull + m % kSlots), (m / kSlots) & 1, a.status);
             };
             // O += P_t V_t; V(t) is the next two ring slots (keys [0,64) and [64,128)); P_t in TMEM
-            // over S buffer t%2: keys [0,64) in columns [0,32), keys [64,128) in [64,96).
+            // over S buffer t%2: keys [0,64) (softmax half 0) in columns [0,32), keys [64,128)
+            // (half 1) in [64,96).  Each half's keys go as soon as that half has written P.
             auto issue_pv = [&](uint32_t t, bool first, uint32_t it) {
                 if (!alive) return;
-                alive = mbar_wait_cluster(bar(kBarP + (t & 1)), (t >> 1) & 1, a.status);
-                if (alive && first && it >= 1) alive = mbar_wait_cluster(bar(kBarOFree), (it - 1) & 1, a.status);
-                if (!alive) return;
-                tc_fence_after();
+                if (first && it >= 1) alive = mbar_wait(bar(kBarOFree), (it - 1) & 1, a.status);
                 const uint32_t p_col = tmem + kColS + (t & 1) * kBN;
-                for (int s = 0; s < 2; ++s) {
+                for (int s = 0; s < 2 && alive; ++s) {
+                    if (!mbar_wait(bar(kBarP + 2 * s + (t & 1)), (t >> 1) & 1, a.status)) {
+                        alive = false;
+                        return;
+                    }
                     if (!wait_full(n)) {
                         alive = false;
                         return;
@@ -294,7 +299,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int idx = items[it % kItemRing];
                 if (idx < 0) break;
                 const Item g = item_geometry(static_cast<uint32_t>(idx), a, 0);
-                if (!mbar_wait_cluster(bar(kBarQFull), it & 1, a.status)) break;
+                if (!mbar_wait(bar(kBarQFull), it & 1, a.status)) break;
                 tc_fence_after();
                 for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
                     const uint32_t t = gt + j;
@@ -332,7 +337,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const uint32_t half = (warp - 4) >> 2, quad = warp & 3;
         const uint32_t r = quad * 32 + lane;                  // query row == TMEM lane
         const uint32_t lane_base = tmem + ((32u * quad) << 16);
-        const uint32_t p_bar0 = mapa(bar(kBarP), 0), p_bar1 = mapa(bar(kBarP + 1), 0);
+        const uint32_t p_bar0 = mapa(bar(kBarP + 2 * half), 0), p_bar1 = mapa(bar(kBarP + 2 * half + 1), 0);
         const uint32_t ofree_bar = mapa(bar(kBarOFree), 0);
         float *red = reinterpret_cast<float *>(base + kOffRed);  // [2 parity][2 half][128]
         uint32_t gt = 0, xchg = 0;
@@ -341,8 +346,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // issued before those S MMAs) and PV(t+2) cannot have started, so the parity is
         // unambiguous without observing every phase.
         auto wait_pv = [&](uint32_t t) {
-            alive = alive &&
-                    __all_sync(0xffffffffu, mbar_wait_cluster(bar(kBarO + (t & 1)), (t >> 1) & 1, a.status));
+            alive = alive && __all_sync(0xffffffffu, mbar_wait(bar(kBarO + (t & 1)), (t >> 1) & 1, a.status));
         };
         auto exchange = [&](float mine, float &theirs) {
             const uint32_t slot = xchg & 1;
@@ -357,7 +361,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         auto warp_arrive = [&](uint32_t cluster_bar) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(cluster_bar);
+            if (lane == 0) mbar_arrive_remote(cluster_bar);
         };
         for (uint32_t it = 0; alive; ++it) {
             if (!__all_sync(0xffffffffu, mbar_wait_cluster(bar(kBarItem + it % kItemRing), (it / kItemRing) & 1,
@@ -373,38 +377,66 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             float m_run = -INFINITY, l_part = 0.f;
             for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
                 const uint32_t tt = gt + j;
-                bool ok = __all_sync(0xffffffffu,
-                                     mbar_wait_cluster(bar(kBarS + (tt & 1)), (tt >> 1) & 1, a.status));
+                if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarS + (tt & 1)), (tt >> 1) & 1, a.status))) {
+                    alive = false;
+                    break;
+                }
                 tc_fence_after();
+                const uint32_t s_row = lane_base + kColS + (tt & 1) * kBN;
+                const uint32_t s_addr = s_row + half * 64;
+                const uint32_t o_addr = s_row + (half ^ 1) * 64;
                 uint32_t sv[64];
-                const uint32_t s_addr = lane_base + kColS + (tt & 1) * kBN + half * 64;
-                if (ok) {
-                    tmem_ld64(s_addr, sv);
+                float mx;
+                {
+                    uint32_t ov[32];
+                    tmem_ld32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+                    tmem_ld32(o_addr, ov);
                     tc_wait_ld();
+                    mx = fmax3(__uint_as_float(ov[0]), __uint_as_float(ov[1]), __uint_as_float(ov[2]));
+#pragma unroll
+                    for (int k = 3; k < 31; k += 2) mx = fmax3(mx, __uint_as_float(ov[k]), __uint_as_float(ov[k + 1]));
+                    mx = fmaxf(mx, __uint_as_float(ov[31]));
+                    tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+                    tmem_ld32(o_addr + 32, ov);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int k = 0; k < 32; k += 2) mx = fmax3(mx, __uint_as_float(ov[k]), __uint_as_float(ov[k + 1]));
                 }
                 const uint32_t tile0 = g.j_start + j * kBN;
                 const bool need_mask = g.rows_valid && ((tile0 + kBN - 1 > g.pos_first) ||
                                                         (a.window && tile0 + a.window <= g.pos_last));
                 if (need_mask) {
-                    // visible keys of this row relative to this half's first key: [lo, hi]
-                    const int key0 = static_cast<int>(tile0 + half * 64);
-                    const int hi = pos - key0;
-                    const int lo = a.window ? pos + 1 - static_cast<int>(a.window) - key0 : -(1 << 30);
+                    // visible keys of this row relative to the tile's first key: [lo, hi]; the
+                    // other half's scores were only read for the max, so mask them in the max
+                    const int hi = pos - static_cast<int>(tile0);
+                    const int lo = a.window ? pos + 1 - static_cast<int>(a.window) - static_cast<int>(tile0)
+                                            : -(1 << 30);
+                    const int own = static_cast<int>(half) * 64;
 #pragma unroll
                     for (int k = 0; k < 64; ++k)
-                        if (k > hi || k < lo) sv[k] = 0xff800000u;  // -inf
-                }
-                float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                        if (own + k > hi || own + k < lo) sv[k] = 0xff800000u;  // -inf
+                    // the unmasked max over both halves: recompute from the visible range only
+                    float vis = -INFINITY;
 #pragma unroll
-                for (int k = 0; k < 64; ++k) mx[k & 3] = fmaxf(mx[k & 3], __uint_as_float(sv[k]));
-                const float mine = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-                float other;
-                ok = exchange(mine, other) && ok;
-                if (!ok) {
-                    alive = false;
-                    break;
+                    for (int k = 0; k < 64; ++k) vis = fmaxf(vis, __uint_as_float(sv[k]));
+                    uint32_t ov[32];
+                    const int oth = static_cast<int>(half ^ 1) * 64;
+#pragma unroll 1
+                    for (int c = 0; c < 2; ++c) {
+                        tmem_ld32(o_addr + 32 * c, ov);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int k = 0; k < 32; ++k) {
+                            const int key = oth + 32 * c + k;
+                            if (key <= hi && key >= lo) vis = fmaxf(vis, __uint_as_float(ov[k]));
+                        }
+                    }
+                    mx = vis;
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 64; k += 2) mx = fmax3(mx, __uint_as_float(sv[k]), __uint_as_float(sv[k + 1]));
                 }
-                const float mt = fmaxf(mine, other) * a.scale_log2;
+                const float mt = mx * a.scale_log2;
                 float alpha = 1.f;
                 bool rescale = false;
                 if (mt > m_run + kTau) {
