@@ -84,6 +84,7 @@ struct PrefillArgs {
     unsigned *status;     // device status word
     unsigned *sched;      // [0] next item, [1] CTAs done (zeroed by the prep kernel)
     uint32_t batch, T, pos0, kv_len, q_heads, kv_heads, window, n_qtiles, n_items, pair_heads;
+    uint32_t group_major;  // items ordered (sequence, heads) first, so concurrent pairs share K/V in L2
     float scale_log2;
 };
 
@@ -93,24 +94,35 @@ struct Item {
     uint32_t j_start, n_tiles;                  // key tiles of the pair
 };
 
+// Item order: heaviest query tiles (most keys) first across all (sequence, heads) when the
+// launch's K/V fits in L2 many times over; otherwise (sequence, heads) major with the query tiles
+// of one group taken together, heaviest first, so the pairs that run at once stream the same keys.
+__device__ __forceinline__ void split_item(uint32_t idx, uint32_t groups, const PrefillArgs &a, uint32_t &qt,
+                                           uint32_t &grp) {
+    if (a.group_major) {
+        grp = idx / a.n_qtiles;
+        qt = a.n_qtiles - 1 - idx % a.n_qtiles;
+    } else {
+        qt = a.n_qtiles - 1 - idx / groups;
+        grp = idx % groups;
+    }
+}
+
 __device__ __forceinline__ Item item_geometry(uint32_t idx, const PrefillArgs &a, uint32_t rank) {
     Item it;
-    uint32_t t0_pair, span;
+    uint32_t t0_pair, span, qt, bp;
     if (a.pair_heads) {  // two heads of one GQA group, same 128 queries
-        const uint32_t pairs = a.q_heads / 2, per_tile = a.batch * pairs;
-        const uint32_t qt = a.n_qtiles - 1 - idx / per_tile;  // last query tiles (most keys) first
-        const uint32_t bp = idx % per_tile;
+        const uint32_t pairs = a.q_heads / 2;
+        split_item(idx, a.batch * pairs, a, qt, bp);
         it.b = bp / pairs;
         it.h = 2 * (bp % pairs) + rank;
         t0_pair = qt * kBM;
         it.t0 = t0_pair;
         span = kBM;
     } else {  // one head, 256 consecutive queries
-        const uint32_t per_tile = a.batch * a.q_heads;
-        const uint32_t qt = a.n_qtiles - 1 - idx / per_tile;
-        const uint32_t bh = idx % per_tile;
-        it.b = bh / a.q_heads;
-        it.h = bh % a.q_heads;
+        split_item(idx, a.batch * a.q_heads, a, qt, bp);
+        it.b = bp / a.q_heads;
+        it.h = bp % a.q_heads;
         t0_pair = qt * 2 * kBM;
         it.t0 = t0_pair + rank * kBM;
         span = 2 * kBM;
@@ -260,6 +272,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (leader && lane == 0) {
             constexpr uint32_t idS = idesc_bf16_f32(2 * kBM, kBN, 0, 0);
             constexpr uint32_t idPV = idesc_bf16_f32(2 * kBM, kD, 0, 1);
+            // Descriptors of the first K-step; every other step is a byte offset added to the
+            // start-address field (address >> 4, all offsets stay inside shared memory).
+            const uint64_t q_desc = smem_desc_sw128(sb + kOffQ, 16, 1024);
+            const uint64_t k_desc = smem_desc_sw128(sb + kOffSlots, 16, 1024);
+            const uint64_t v_desc = smem_desc_sw128(sb + kOffSlots, kChunk, 1024);
             uint32_t gt = 0, n = 0;
             auto wait_full = [&](uint32_t m) {
                 return mbar_wait(bar(kBarFull + m % kSlots), (m / kSlots) & 1, a.status);
@@ -282,13 +299,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t slot = n % kSlots;
+                    const uint64_t vd = v_desc + ((slot * kSlotBytes) >> 4);
 #pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) {
-                        const uint64_t bd =
-                            smem_desc_sw128(sb + kOffSlots + slot * kSlotBytes + ks * 2048, kChunk, 1024);
-                        tc_mma_ts_pair(tmem + kColO, p_col + s * 64 + ks * 8, bd, idPV,
+                    for (int ks = 0; ks < 4; ++ks)
+                        tc_mma_ts_pair(tmem + kColO, p_col + s * 64 + ks * 8, vd + ((ks * 2048) >> 4), idPV,
                                        (!first || s > 0 || ks > 0) ? 1u : 0u);
-                    }
                     tc_commit_pair_both(bar(kBarEmpty + slot));
                     ++n;
                 }
@@ -311,14 +326,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                         tc_fence_after();
                         const uint32_t slot = n % kSlots;
+                        const uint64_t kd = k_desc + ((slot * kSlotBytes) >> 4);
+                        const uint64_t qd = q_desc + ((s * 2 * (kQBytes / 4)) >> 4);
 #pragma unroll
-                        for (int ks = 0; ks < 8; ++ks) {
-                            const int kk = 8 * s + ks;  // 16-dim step of the 256 dims
-                            const uint64_t ad = smem_desc_sw128(sb + kOffQ + (kk / 4) * (kQBytes / 4) + (kk % 4) * 32,
-                                                                16, 1024);
-                            const uint64_t bd = smem_desc_sw128(
-                                sb + kOffSlots + slot * kSlotBytes + (ks / 4) * kChunk + (ks % 4) * 32, 16, 1024);
-                            tc_mma_ss_pair(s_col, ad, bd, idS, kk > 0 ? 1u : 0u);
+                        for (int ks = 0; ks < 8; ++ks) {  // 16-dim step 8s + ks of the 256 dims
+                            const uint32_t off = ((ks / 4) * (kQBytes / 4) + (ks % 4) * 32) >> 4;
+                            const uint32_t koff = ((ks / 4) * kChunk + (ks % 4) * 32) >> 4;
+                            tc_mma_ss_pair(s_col, qd + off, kd + koff, idS, (s | ks) ? 1u : 0u);
                         }
                         tc_commit_pair_both(bar(kBarEmpty + slot));
                         ++n;
@@ -775,6 +789,9 @@ int launch_attend(const apex_attn_params *p, void *workspace, const uint16_t *k_
         fa.n_items = batch * p->q_heads * fa.n_qtiles;
     }
     fa.scale_log2 = p->scale * kLog2e;
+    // K and V of the whole launch: beyond ~3/8 of L2, order items so that pairs share keys
+    const uint64_t kv_bytes = kv_rows * kv_len * kD * 2 * 2;
+    fa.group_major = kv_bytes > (48ull << 20);
     const uint32_t pairs = std::min<uint32_t>(fa.n_items, max_active_pairs());
     prefill_pair_kernel<<<2 * pairs, kThreads, kSmemBytes, s>>>(tq, tk, tv, fa);
     return check_cuda(cudaGetLastError(), "prefill attention launch");
