@@ -561,36 +561,51 @@ struct PrepArgs {
     RopeTable rope;
 };
 
-// RMSNorm (optional, weight in registers) + RoPE with this lane's precomputed cos/sin of one
-// 256-wide row held 8 dims per lane; pairs (i, i+128) meet across lanes l and l^16.
-__device__ __forceinline__ void norm_rope_cs(float (&x)[8], uint32_t lane, bool norm, const float (&w)[8],
-                                             float eps, bool rope, uint32_t rope_pairs, const float (&cs)[8],
-                                             const float (&sn)[8]) {
+// Prep work unit = (token, group): groups [0, nqg) are 8 q heads each, groups [nqg, nqg + nkg)
+// are 4 kv heads each (k and v).  A warp issues all loads of its unit (4 KB) before any math.
+// Lane l holds dims [4l, 4l+4) and [128+4l, 128+4l+4) of each row: both members of its four RoPE
+// pairs, so rotation needs no shuffles and each lane computes only its own four cos/sin.
+constexpr int kPrepThreads = 256;
+
+// RMS norm (optional) with this lane's 8 weights, then RoPE over its 4 pairs (lo[i], hi[i]).
+__device__ __forceinline__ void norm_rope_pairs(float (&lo)[4], float (&hi)[4], bool norm, const float (&w)[8],
+                                                float eps, uint32_t pair0, uint32_t rope_pairs, const float (&c)[4],
+                                                const float (&sn)[4]) {
     if (norm) {
         float ss = 0.f;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
+        for (int e = 0; e < 4; ++e) ss += lo[e] * lo[e] + hi[e] * hi[e];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         const float inv = 1.0f / sqrtf(ss / static_cast<float>(kD) + eps);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = x[e] * inv * w[e];
-    }
-    if (rope) {
-        const bool low = lane < 16;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
-            if (8 * (lane & 15) + e < rope_pairs)
-                x[e] = low ? (x[e] * cs[e] - other * sn[e]) : (other * sn[e] + x[e] * cs[e]);
+        for (int e = 0; e < 4; ++e) {
+            lo[e] = lo[e] * inv * w[e];
+            hi[e] = hi[e] * inv * w[4 + e];
         }
     }
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+        if (pair0 + e < rope_pairs) {
+            const float l = lo[e], h = hi[e];
+            lo[e] = l * c[e] - h * sn[e];
+            hi[e] = h * c[e] + l * sn[e];
+        }
 }
 
-// Work unit = (position, group): groups [0, nqg) are 8 q heads each, groups [nqg, nqg + nkg)
-// are 4 kv heads each (k and v); a warp issues all loads of its unit before any math, so one
-// HBM round trip covers 8 rows and many units are in flight per SM.
-__global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant__ PrepArgs a) {
+__device__ __forceinline__ void unpack4(uint2 v, float (&x)[4]) {
+    x[0] = bf16lo(v.x); x[1] = bf16hi(v.x); x[2] = bf16lo(v.y); x[3] = bf16hi(v.y);
+}
+__device__ __forceinline__ uint2 pack4(const float (&x)[4]) { return make_uint2(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3])); }
+
+// cos and sin of the f32 angle pos * inv_freq: single precision where its argument reduction is
+// exact (|angle| below 1e5), double precision beyond (long contexts).
+__device__ __forceinline__ void rope_sincos(float angle, float &s, float &c) {
+    if (fabsf(angle) < 1.0e5f) sincosf(angle, &s, &c);
+    else sincos_angle(angle, s, c);
+}
+
+__global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid_constant__ PrepArgs a) {
     const uint32_t lane = threadIdx.x & 31;
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         a.sched[0] = 0;
@@ -599,6 +614,7 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
     const uint32_t nqg = (a.q_heads + 7) / 8, nkg = (a.kv_heads + 3) / 4, groups = nqg + nkg;
     const uint64_t units = static_cast<uint64_t>(a.B) * a.T * groups;
     const uint64_t warps = static_cast<uint64_t>(gridDim.x) * (blockDim.x >> 5);
+    const uint32_t d_lo = 4 * lane, d_hi = kD / 2 + 4 * lane;
     for (uint64_t u = static_cast<uint64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); u < units;
          u += warps) {
         const uint64_t bt = u / groups;
@@ -607,55 +623,66 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
         const bool is_q = grp < nqg;
         const uint32_t h0 = is_q ? grp * 8 : (grp - nqg) * 4;
         const uint32_t n = is_q ? min(8u, a.q_heads - h0) : min(4u, a.kv_heads - h0);
-        uint4 raw[8];
+        uint2 raw[8][2];
         if (is_q) {
-            const uint16_t *src = a.q_raw + (bt * a.q_heads + h0) * kD + 8 * lane;
+            const uint16_t *src = a.q_raw + (bt * a.q_heads + h0) * kD;
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-                if (static_cast<uint32_t>(i) < n) raw[i] = *reinterpret_cast<const uint4 *>(src + i * kD);
+                if (static_cast<uint32_t>(i) < n) {
+                    raw[i][0] = *reinterpret_cast<const uint2 *>(src + i * kD + d_lo);
+                    raw[i][1] = *reinterpret_cast<const uint2 *>(src + i * kD + d_hi);
+                }
         } else {
-            const uint16_t *ks = a.k_raw + (bt * a.kv_heads + h0) * kD + 8 * lane;
-            const uint16_t *vs = a.v_raw + (bt * a.kv_heads + h0) * kD + 8 * lane;
+            const uint16_t *ks = a.k_raw + (bt * a.kv_heads + h0) * kD;
+            const uint16_t *vs = a.v_raw + (bt * a.kv_heads + h0) * kD;
 #pragma unroll
             for (int i = 0; i < 4; ++i)
                 if (static_cast<uint32_t>(i) < n) {
-                    raw[i] = *reinterpret_cast<const uint4 *>(ks + i * kD);
-                    raw[4 + i] = *reinterpret_cast<const uint4 *>(vs + i * kD);
+                    raw[i][0] = *reinterpret_cast<const uint2 *>(ks + i * kD + d_lo);
+                    raw[i][1] = *reinterpret_cast<const uint2 *>(ks + i * kD + d_hi);
+                    raw[4 + i][0] = *reinterpret_cast<const uint2 *>(vs + i * kD + d_lo);
+                    raw[4 + i][1] = *reinterpret_cast<const uint2 *>(vs + i * kD + d_hi);
                 }
         }
         const float pos = static_cast<float>(a.pos0 + t);
-        float cs[8], sn[8], w[8], ones[8];
+        float cs[4], sn[4], w[8];
         const uint16_t *wsrc = is_q ? a.q_w : a.k_w;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const uint32_t i = 8 * (lane & 15) + e;
-            if (i < a.rope_pairs) sincos_angle(pos * a.rope.inv_freq[i], sn[e], cs[e]);
+        for (int e = 0; e < 4; ++e) {
+            if (d_lo + e < a.rope_pairs) rope_sincos(pos * a.rope.inv_freq[d_lo + e], sn[e], cs[e]);
             else cs[e] = 1.f, sn[e] = 0.f;
-            w[e] = wsrc ? __uint_as_float(static_cast<uint32_t>(wsrc[8 * lane + e]) << 16) : 1.0f;
-            ones[e] = 1.0f;
+            w[e] = wsrc ? __uint_as_float(static_cast<uint32_t>(wsrc[d_lo + e]) << 16) : 1.0f;
+            w[4 + e] = wsrc ? __uint_as_float(static_cast<uint32_t>(wsrc[d_hi + e]) << 16) : 1.0f;
         }
         if (is_q) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 if (static_cast<uint32_t>(i) >= n) break;
-                float x[8];
-                unpack8(raw[i], x);
-                norm_rope_cs(x, lane, a.qk_norm, w, a.eps, a.rope_pairs != 0, a.rope_pairs, cs, sn);
+                float lo[4], hi[4];
+                unpack4(raw[i][0], lo);
+                unpack4(raw[i][1], hi);
+                norm_rope_pairs(lo, hi, a.qk_norm, w, a.eps, d_lo, a.rope_pairs, cs, sn);
                 uint16_t *dst = a.q_ws + ((static_cast<uint64_t>(b) * a.q_heads + h0 + i) * a.T + t) * kD;
-                *reinterpret_cast<uint4 *>(dst + 8 * lane) = pack8(x);
+                *reinterpret_cast<uint2 *>(dst + d_lo) = pack4(lo);
+                *reinterpret_cast<uint2 *>(dst + d_hi) = pack4(hi);
             }
         } else {
+            const float ones[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 if (static_cast<uint32_t>(i) >= n) break;
                 const uint64_t off = ((static_cast<uint64_t>(b) * a.kv_heads + h0 + i) * a.capacity + a.pos0 + t) * kD;
-                float x[8], y[8];
-                unpack8(raw[i], x);
-                unpack8(raw[4 + i], y);
-                norm_rope_cs(x, lane, a.qk_norm, w, a.eps, a.rope_pairs != 0, a.rope_pairs, cs, sn);
-                norm_rope_cs(y, lane, a.v_norm, ones, a.eps, false, 0, cs, sn);
-                *reinterpret_cast<uint4 *>(a.k_cache + off + 8 * lane) = pack8(x);
-                *reinterpret_cast<uint4 *>(a.v_cache + off + 8 * lane) = pack8(y);
+                float klo[4], khi[4], vlo[4], vhi[4];
+                unpack4(raw[i][0], klo);
+                unpack4(raw[i][1], khi);
+                unpack4(raw[4 + i][0], vlo);
+                unpack4(raw[4 + i][1], vhi);
+                norm_rope_pairs(klo, khi, a.qk_norm, w, a.eps, d_lo, a.rope_pairs, cs, sn);
+                norm_rope_pairs(vlo, vhi, a.v_norm, ones, a.eps, 0, 0, cs, sn);
+                *reinterpret_cast<uint2 *>(a.k_cache + off + d_lo) = pack4(klo);
+                *reinterpret_cast<uint2 *>(a.k_cache + off + d_hi) = pack4(khi);
+                *reinterpret_cast<uint2 *>(a.v_cache + off + d_lo) = pack4(vlo);
+                *reinterpret_cast<uint2 *>(a.v_cache + off + d_hi) = pack4(vhi);
             }
         }
     }
@@ -714,8 +741,9 @@ int launch_prep(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t
     pa.eps = p->eps;
     rope_table(pa.rope.inv_freq, p->rope_pairs, kD, p->rope_base);
     const uint64_t units = static_cast<uint64_t>(batch) * tokens * ((p->q_heads + 7) / 8 + (p->kv_heads + 3) / 4);
-    const uint32_t grid = static_cast<uint32_t>(std::max<uint64_t>(1, std::min<uint64_t>((units + 7) / 8, 32ull * sm_count())));
-    prefill_prep_kernel<<<grid, 256, 0, s>>>(pa);
+    const uint32_t grid = static_cast<uint32_t>(
+        std::max<uint64_t>(1, std::min<uint64_t>((units + kPrepThreads / 32 - 1) / (kPrepThreads / 32), 32ull * sm_count())));
+    prefill_prep_kernel<<<grid, kPrepThreads, 0, s>>>(pa);
     return check_cuda(cudaGetLastError(), "prefill prep launch");
 }
 
