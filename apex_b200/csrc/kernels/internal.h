@@ -28,6 +28,12 @@ int make_tensor_map_bf16_3d(CUtensorMap *map, const void *base, uint64_t d0, uin
                             uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
                             uint32_t box0, uint32_t box1);
 
+// A 4-D bf16 tensor map with 64-byte swizzle, for tiled stores of 32-element (64-byte) rows:
+// dims {d0 (innermost), d1, d2, d3}, byte strides of dims 1..3, box {box0, box1, box2, box3}.
+// Elements outside the tensor are not written.
+int make_tensor_map_bf16_4d_sw64(CUtensorMap *map, const void *base, const uint64_t (&dims)[4],
+                                 const uint64_t (&strides_bytes)[3], const uint32_t (&box)[4]);
+
 // inv_freq[i] = base^(-2i/head_dim) (f32 exponent, double-precision power rounded to f32) for
 // i < pairs, the frequencies of shaders/head_norm_rope.metal:59.
 void rope_table(float *inv_freq, uint32_t pairs, uint32_t head_dim, float base);

@@ -47,13 +47,15 @@ namespace {
 constexpr int kD = 256;
 constexpr int kBM = 128;                             // query rows per CTA
 constexpr int kBN = 128;                             // keys per tile (both CTAs)
-constexpr int kSlots = 10;
+constexpr int kSlots = 9;
 constexpr uint32_t kChunk = 64 * 128;                // 64 rows x 128 B (one TMA box)
 constexpr uint32_t kSlotBytes = 2 * kChunk;          // 16 KB
 constexpr uint32_t kQBytes = kBM * kD * 2;           // 64 KB
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffSlots = kQBytes;
-constexpr uint32_t kOffBar = kOffSlots + kSlots * kSlotBytes;
+constexpr uint32_t kOffStage = kOffSlots + kSlots * kSlotBytes;  // epilogue staging: 8 warps x [32 rows][64 B]
+constexpr uint32_t kStageWarpBytes = 32 * 64;
+constexpr uint32_t kOffBar = kOffStage + 8 * kStageWarpBytes;
 constexpr uint32_t kNumBars = 48;
 constexpr uint32_t kOffItems = kOffBar + 8 * kNumBars;
 constexpr uint32_t kItemRing = 8;
@@ -70,6 +72,7 @@ constexpr uint32_t kPairWarps = 16;                  // softmax warps of both CT
 constexpr uint32_t kHalfWarps = 8;                   // one softmax half of both CTAs
 
 static_assert(kSmemBytes <= 232448, "shared memory budget");
+static_assert(kOffStage % 1024 == 0, "64-byte-swizzled staging tiles need 512-byte alignment");
 
 // barrier indices (8 bytes each at kOffBar).  CTA 0's copies of QFull, Full, P and OFree count
 // the pair; Empty, QEmpty, S and O are signalled in both CTAs by multicast commits.  P is one
@@ -108,6 +111,15 @@ __device__ __forceinline__ void split_item(uint32_t idx, uint32_t groups, const 
     }
 }
 
+// Bit k set for k in [lo, hi] (bounds relative to a 32-key chunk; empty when hi < lo).
+__device__ __forceinline__ uint32_t visible_bits(int lo, int hi) {
+    lo = max(lo, 0);
+    hi = min(hi, 31);
+    if (hi < lo) return 0u;
+    const uint32_t upto_hi = hi == 31 ? 0xffffffffu : ((2u << hi) - 1u);
+    return upto_hi & ~((1u << lo) - 1u);
+}
+
 __device__ __forceinline__ Item item_geometry(uint32_t idx, const PrefillArgs &a, uint32_t rank) {
     Item it;
     uint32_t t0_pair, span, qt, bp;
@@ -142,7 +154,8 @@ __device__ __forceinline__ Item item_geometry(uint32_t idx, const PrefillArgs &a
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     prefill_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const PrefillArgs a) {
+                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                        const PrefillArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *base = smem_raw;
     const uint32_t sb = smem_u32(base);
@@ -193,6 +206,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             prefetch_tensormap(&tm_q);
             prefetch_tensormap(&tm_k);
             prefetch_tensormap(&tm_v);
+            // Everything above overlapped the preceding kernel (the prep); from here on this
+            // thread reads its outputs (scheduler counters, q, K, V), and every other role only
+            // acts on items and data this thread hands on.
+            griddep_wait();
             uint32_t n = 0;  // ring position (same sequence in both CTAs and the MMA issuer)
             auto next_slot = [&](uint32_t &dst, uint32_t &full) {
                 const uint32_t slot = n % kSlots;
@@ -402,53 +419,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 uint32_t sv[64];
                 float mx;
                 {
-                    uint32_t ov[32];
-                    tmem_ld32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-                    tmem_ld32(o_addr, ov);
-                    tc_wait_ld();
-                    mx = fmax3(__uint_as_float(ov[0]), __uint_as_float(ov[1]), __uint_as_float(ov[2]));
-#pragma unroll
-                    for (int k = 3; k < 31; k += 2) mx = fmax3(mx, __uint_as_float(ov[k]), __uint_as_float(ov[k + 1]));
-                    mx = fmaxf(mx, __uint_as_float(ov[31]));
-                    tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-                    tmem_ld32(o_addr + 32, ov);
-                    tc_wait_ld();
-#pragma unroll
-                    for (int k = 0; k < 32; k += 2) mx = fmax3(mx, __uint_as_float(ov[k]), __uint_as_float(ov[k + 1]));
-                }
-                const uint32_t tile0 = g.j_start + j * kBN;
-                const bool need_mask = g.rows_valid && ((tile0 + kBN - 1 > g.pos_first) ||
-                                                        (a.window && tile0 + a.window <= g.pos_last));
-                if (need_mask) {
-                    // visible keys of this row relative to the tile's first key: [lo, hi]; the
-                    // other half's scores were only read for the max, so mask them in the max
+                    const uint32_t tile0 = g.j_start + j * kBN;
+                    const bool need_mask = g.rows_valid && ((tile0 + kBN - 1 > g.pos_first) ||
+                                                            (a.window && tile0 + a.window <= g.pos_last));
+                    // visible keys of this row relative to the tile's first key: [lo, hi]
                     const int hi = pos - static_cast<int>(tile0);
-                    const int lo = a.window ? pos + 1 - static_cast<int>(a.window) - static_cast<int>(tile0)
-                                            : -(1 << 30);
-                    const int own = static_cast<int>(half) * 64;
-#pragma unroll
-                    for (int k = 0; k < 64; ++k)
-                        if (own + k > hi || own + k < lo) sv[k] = 0xff800000u;  // -inf
-                    // the unmasked max over both halves: recompute from the visible range only
-                    float vis = -INFINITY;
-#pragma unroll
-                    for (int k = 0; k < 64; ++k) vis = fmaxf(vis, __uint_as_float(sv[k]));
+                    const int lo = a.window ? pos + 1 - static_cast<int>(a.window) - static_cast<int>(tile0) : -(1 << 30);
+                    const int own = static_cast<int>(half) * 64, oth = static_cast<int>(half ^ 1) * 64;
                     uint32_t ov[32];
-                    const int oth = static_cast<int>(half ^ 1) * 64;
-#pragma unroll 1
+                    mx = -INFINITY;
+#pragma unroll
                     for (int c = 0; c < 2; ++c) {
+                        uint32_t(&sc)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[32 * c]);
+                        tmem_ld32(s_addr + 32 * c, sc);
                         tmem_ld32(o_addr + 32 * c, ov);
-                        tc_wait_ld();
+                        tc_wait_ld(sc, ov);
+                        if (need_mask) {
+                            const uint32_t vo = visible_bits(lo - own - 32 * c, hi - own - 32 * c);
+                            const uint32_t vx = visible_bits(lo - oth - 32 * c, hi - oth - 32 * c);
 #pragma unroll
-                        for (int k = 0; k < 32; ++k) {
-                            const int key = oth + 32 * c + k;
-                            if (key <= hi && key >= lo) vis = fmaxf(vis, __uint_as_float(ov[k]));
+                            for (int k = 0; k < 32; ++k) {
+                                if (!((vo >> k) & 1u)) sc[k] = 0xff800000u;  // -inf
+                                if (!((vx >> k) & 1u)) ov[k] = 0xff800000u;
+                            }
                         }
-                    }
-                    mx = vis;
-                } else {
 #pragma unroll
-                    for (int k = 0; k < 64; k += 2) mx = fmax3(mx, __uint_as_float(sv[k]), __uint_as_float(sv[k + 1]));
+                        for (int k = 0; k < 32; k += 2) mx = fmax3(mx, __uint_as_float(ov[k]), __uint_as_float(ov[k + 1]));
+#pragma unroll
+                        for (int k = 0; k < 32; k += 2) mx = fmax3(mx, __uint_as_float(sc[k]), __uint_as_float(sc[k + 1]));
+                    }
                 }
                 const float mt = mx * a.scale_log2;
                 float alpha = 1.f;
@@ -481,7 +480,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         uint32_t o[32];
                         const uint32_t oa = lane_base + kColO + half * 128 + c * 32;
                         tmem_ld32(oa, o);
-                        tc_wait_ld();
+                        tc_wait_ld(o);
 #pragma unroll
                         for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
                         tmem_st32(oa, o);
@@ -502,32 +501,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const float l_run = l_part + l_other;
             const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
-            const bool row_valid = r < g.rows_valid;
-            uint16_t *orow = a.out + ((static_cast<uint64_t>(g.b) * a.T + t) * a.q_heads + g.h) * kD + half * 128;
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                uint32_t o[32];
-                tmem_ld32(lane_base + kColO + half * 128 + c * 32, o);
-                tc_wait_ld();
-                if (row_valid) {
-                    uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 32);
+            // Each 32-column chunk of this warp's 32 rows goes to global memory as one TMA store
+            // from a 2 KB staging tile ([32 rows][64 B], 64-byte swizzle: 16-byte piece q of row x
+            // at ((q ^ ((x >> 1) & 3)) * 16)); rows at or past T are clipped by the tensor map.
+            uint8_t *stg = base + kOffStage + (warp - 4) * kStageWarpBytes;
+            const bool any_rows = quad * 32 < g.rows_valid;
+            uint32_t ob[2][32];  // chunk c is packed while chunk c + 1 is read from TMEM
+            tmem_ld32(lane_base + kColO + half * 128, ob[0]);
+            tc_wait_ld(ob[0]);
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        uint4 v;
-                        v.x = pack_bf16(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l);
-                        v.y = pack_bf16(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l);
-                        v.z = pack_bf16(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
-                        v.w = pack_bf16(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
-                        dst[q] = v;
-                    }
+            for (int c = 0; c < 4; ++c) {
+                uint32_t(&o)[32] = ob[c & 1];
+                if (c < 3) tmem_ld32(lane_base + kColO + half * 128 + (c + 1) * 32, ob[(c + 1) & 1]);
+                uint4 v[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    v[q].x = pack_bf16(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l);
+                    v[q].y = pack_bf16(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l);
+                    v[q].z = pack_bf16(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
+                    v[q].w = pack_bf16(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
                 }
+                if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging tile
+                __syncwarp();
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<uint4 *>(stg + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = v[q];
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && any_rows) {
+                    tma_store_4d(&tm_o, smem_u32(stg), static_cast<int32_t>(half * 128 + c * 32),
+                                 static_cast<int32_t>(g.h), static_cast<int32_t>(g.t0 + quad * 32),
+                                 static_cast<int32_t>(g.b));
+                    bulk_commit_group();
+                }
+                if (c < 3) tc_wait_ld(ob[(c + 1) & 1]);
             }
             warp_arrive(ofree_bar);
             gt += g.n_tiles;
         }
     }
-    // Teardown.  After a failed wait, copies or MMAs of this pair may still be in flight: give them
-    // time to land (bounded) before the pair releases TMEM and shared memory.
+    // Teardown.  The epilogue's TMA stores finish first.  After a failed wait, copies or MMAs of
+    // this pair may still be in flight: give them time to land (bounded) before the pair releases
+    // TMEM and shared memory.
+    if (warp >= 4 && lane == 0) bulk_wait_all();
     if (!alive) *err_flag = 1u;
     __syncwarp();
     tc_fence_before();
@@ -607,6 +623,7 @@ __device__ __forceinline__ void rope_sincos(float angle, float &s, float &c) {
 
 __global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid_constant__ PrepArgs a) {
     const uint32_t lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) griddep_launch_dependents();  // the attention kernel's set-up may start
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         a.sched[0] = 0;
         a.sched[1] = 0;
@@ -791,6 +808,12 @@ int launch_attend(const apex_attn_params *p, void *workspace, const uint16_t *k_
     rc = make_tensor_map_bf16_3d(&tv, v_cache, kD, kv_len, kv_rows, kD * 2ull, static_cast<uint64_t>(capacity) * kD * 2,
                                  64, 64);
     if (rc) return rc;
+    // output [B][T][Hq][256] as {256, Hq, T, B}: one box = 32 dims x 1 head x 32 queries
+    CUtensorMap to;
+    const uint64_t row = static_cast<uint64_t>(kD) * 2;
+    rc = make_tensor_map_bf16_4d_sw64(&to, out, {static_cast<uint64_t>(kD), p->q_heads, tokens, batch},
+                                      {row, row * p->q_heads, row * p->q_heads * tokens}, {32, 1, 32, 1});
+    if (rc) return rc;
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -821,8 +844,19 @@ int launch_attend(const apex_attn_params *p, void *workspace, const uint16_t *k_
     const uint64_t kv_bytes = kv_rows * kv_len * kD * 2 * 2;
     fa.group_major = kv_bytes > (48ull << 20);
     const uint32_t pairs = std::min<uint32_t>(fa.n_items, max_active_pairs());
-    prefill_pair_kernel<<<2 * pairs, kThreads, kSmemBytes, s>>>(tq, tk, tv, fa);
-    return check_cuda(cudaGetLastError(), "prefill attention launch");
+    // Programmatic stream serialization: the pairs' set-up (barriers, TMEM, tensor maps) overlaps
+    // the tail of the preceding kernel; the producers wait for it before touching its outputs.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, prefill_pair_kernel, tq, tk, tv, to, fa), "prefill attention launch");
 }
 
 }  // namespace
