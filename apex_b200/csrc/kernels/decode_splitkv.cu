@@ -66,7 +66,7 @@ struct __align__(16) DecodeSmem {
     float q[kG][kD];
     uint16_t new_k[kD];
     uint16_t new_v[kD];
-    float inv_freq[kD / 2];
+    float rope_cs[kD / 2], rope_sn[kD / 2];  // cos, sin of the new position per pair
     float wm[kConsumerWarps][kG], wl[kConsumerWarps][kG];
     float red[kConsumerWarps][kG];
     uint64_t full[kStages], empty[kStages];
@@ -257,9 +257,12 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
     }
 
     // -------------------------------------------------------------------- consumers
-    for (uint32_t i = tid; i < a.rope_pairs; i += kConsumerWarps * 32) sm.inv_freq[i] = a.rope.inv_freq[i];
-    consumer_sync();
+    // cos/sin of the new position, one pair per consumer thread: the per-row code below stays
+    // small (these short-lived CTAs run it once, so its instruction fetch is on the critical path)
     const float pos_f = static_cast<float>(pos_new);
+    for (uint32_t i = tid; i < a.rope_pairs; i += kConsumerWarps * 32)
+        rope_sincos(pos_f * a.rope.inv_freq[i], sm.rope_sn[i], sm.rope_cs[i]);
+    consumer_sync();
     if (warp < kG) {
         // q of head kvh*G + warp: norm + rope at the new position, pre-scaled for exp2.
         const uint32_t h = kvh * kG + warp;
@@ -267,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
             a.q_raw + (static_cast<uint64_t>(b) * Hq + h) * kD + 8 * lane);
         float x[8];
         unpack8(raw, x);
-        norm_rope_row(x, lane, a.qk_norm, a.q_w, a.eps, a.rope_pairs, sm.inv_freq, pos_f);
+        norm_rope_row_tab(x, lane, a.qk_norm, a.q_w, a.eps, a.rope_pairs, sm.rope_cs, sm.rope_sn);
 #pragma unroll
         for (int e = 0; e < 8; ++e) sm.q[warp][8 * lane + e] = x[e] * a.scale_log2;
     } else if (has_new) {
@@ -279,9 +282,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
         float x[8];
         unpack8(raw, x);
         if (is_k)
-            norm_rope_row(x, lane, a.qk_norm, a.k_w, a.eps, a.rope_pairs, sm.inv_freq, pos_f);
+            norm_rope_row_tab(x, lane, a.qk_norm, a.k_w, a.eps, a.rope_pairs, sm.rope_cs, sm.rope_sn);
         else
-            norm_rope_row(x, lane, a.v_norm, nullptr, a.eps, 0, sm.inv_freq, pos_f);
+            norm_rope_row_tab(x, lane, a.v_norm, nullptr, a.eps, 0, sm.rope_cs, sm.rope_sn);
         const uint4 packed = pack8(x);
         *reinterpret_cast<uint4 *>((is_k ? sm.new_k : sm.new_v) + 8 * lane) = packed;
         uint16_t *dst = (is_k ? a.k_cache : a.v_cache) + head_base +
@@ -387,9 +390,11 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
         mine[kD] = M;
         mine[kD + 1] = den;
     }
-    __threadfence();
     consumer_sync();
     if (tid == 0) {
+        // the barrier orders every consumer's partial before this thread's release fence, which
+        // then publishes them all to the CTA that sees the count complete
+        __threadfence();
         unsigned *counter = a.ws_count + static_cast<uint64_t>(b) * a.kv_heads + kvh;
         const unsigned prev = atomicAdd(counter, 1u);
         const int last = prev == nsplit - 1;
@@ -432,12 +437,12 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
     const float *wg = ms + g * nsplit;
     float r[4] = {0.f, 0.f, 0.f, 0.f};
     uint32_t s = 0;
-    for (; s + 4 <= nsplit; s += 4) {
-        float4 ov[4];
+    for (; s + 8 <= nsplit; s += 8) {  // 8 independent 16-byte loads in flight per thread
+        float4 ov[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) ov[u] = __ldcg(reinterpret_cast<const float4 *>(pg + (s + u) * kWsRec));
+        for (int u = 0; u < 8; ++u) ov[u] = __ldcg(reinterpret_cast<const float4 *>(pg + (s + u) * kWsRec));
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 8; ++u) {
             const float wt = wg[s + u];
             r[0] += wt * ov[u].x;
             r[1] += wt * ov[u].y;

@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32)
         const float pos = static_cast<float>(abs_pos + token);
         for (uint32_t i = lane; i < rope_pairs; i += 32) {
             float s, c;
-            sincos_angle(pos * inv_freq[i], s, c);
+            rope_sincos(pos * inv_freq[i], s, c);
             const float a = row[i], b = row[half + i];
             row[i] = a * c - b * s;
             row[half + i] = a * s + b * c;

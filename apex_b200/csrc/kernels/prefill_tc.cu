@@ -614,13 +614,6 @@ __device__ __forceinline__ void unpack4(uint2 v, float (&x)[4]) {
 }
 __device__ __forceinline__ uint2 pack4(const float (&x)[4]) { return make_uint2(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3])); }
 
-// cos and sin of the f32 angle pos * inv_freq: single precision where its argument reduction is
-// exact (|angle| below 1e5), double precision beyond (long contexts).
-__device__ __forceinline__ void rope_sincos(float angle, float &s, float &c) {
-    if (fabsf(angle) < 1.0e5f) sincosf(angle, &s, &c);
-    else sincos_angle(angle, s, c);
-}
-
 __global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid_constant__ PrepArgs a) {
     const uint32_t lane = threadIdx.x & 31;
     if (threadIdx.x == 0) griddep_launch_dependents();  // the attention kernel's set-up may start

@@ -24,11 +24,11 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
     return v;
 }
 
-// RMSNorm over the 256 dims (if `norm`; weight w is bf16 [256] or null = 1.0), then RoPE of
-// the first rope_pairs pairs at position `pos` (inv_freq[i] = base^(-2i/256)).
-__device__ __forceinline__ void norm_rope_row(float (&x)[8], uint32_t lane, bool norm,
-                                              const uint16_t *w, float eps, uint32_t rope_pairs,
-                                              const float *inv_freq, float pos) {
+// RMSNorm (optional; weight bf16 `w`, or 1 when null) and RoPE of one 256-wide row held 8 dims per
+// lane; pair (i, i + 128) meets across lanes l and l ^ 16.  cos/sin of every pair come from tables
+// (cs[i], sn[i] for i < rope_pairs) computed beforehand.
+__device__ __forceinline__ void norm_rope_row_tab(float (&x)[8], uint32_t lane, bool norm, const uint16_t *w,
+                                                  float eps, uint32_t rope_pairs, const float *cs, const float *sn) {
     if (norm) {
         float ss = 0.f;
 #pragma unroll
@@ -51,11 +51,7 @@ __device__ __forceinline__ void norm_rope_row(float (&x)[8], uint32_t lane, bool
         for (int e = 0; e < 8; ++e) {
             const uint32_t i = 8 * (lane & 15) + e;
             const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
-            if (i < rope_pairs) {
-                float s, c;
-                sincos_angle(pos * inv_freq[i], s, c);
-                x[e] = low ? (x[e] * c - other * s) : (other * s + x[e] * c);
-            }
+            if (i < rope_pairs) x[e] = low ? (x[e] * cs[i] - other * sn[i]) : (other * sn[i] + x[e] * cs[i]);
         }
     }
 }
