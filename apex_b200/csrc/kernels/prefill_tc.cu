@@ -583,37 +583,14 @@ struct PrepArgs {
 // pairs, so rotation needs no shuffles and each lane computes only its own four cos/sin.
 constexpr int kPrepThreads = 256;
 
-// RMS norm (optional) with this lane's 8 weights, then RoPE over its 4 pairs (lo[i], hi[i]).
-__device__ __forceinline__ void norm_rope_pairs(float (&lo)[4], float (&hi)[4], bool norm, const float (&w)[8],
-                                                float eps, uint32_t pair0, uint32_t rope_pairs, const float (&c)[4],
-                                                const float (&sn)[4]) {
-    if (norm) {
-        float ss = 0.f;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) ss += lo[e] * lo[e] + hi[e] * hi[e];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float inv = 1.0f / sqrtf(ss / static_cast<float>(kD) + eps);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            lo[e] = lo[e] * inv * w[e];
-            hi[e] = hi[e] * inv * w[4 + e];
-        }
-    }
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-        if (pair0 + e < rope_pairs) {
-            const float l = lo[e], h = hi[e];
-            lo[e] = l * c[e] - h * sn[e];
-            hi[e] = h * c[e] + l * sn[e];
-        }
-}
-
 __device__ __forceinline__ void unpack4(uint2 v, float (&x)[4]) {
     x[0] = bf16lo(v.x); x[1] = bf16hi(v.x); x[2] = bf16lo(v.y); x[3] = bf16hi(v.y);
 }
 __device__ __forceinline__ uint2 pack4(const float (&x)[4]) { return make_uint2(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3])); }
 
+// One warp per unit.  Lane l holds dims [4l, 4l+4) and [128+4l, 128+4l+4) of each of the unit's 8
+// rows (8 q rows, or 4 k rows then 4 v rows): all loads are issued first, then the 8 rows' RMS
+// reductions run interleaved, then each row is scaled, roped and stored.
 __global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid_constant__ PrepArgs a) {
     const uint32_t lane = threadIdx.x & 31;
     if (threadIdx.x == 0) griddep_launch_dependents();  // the attention kernel's set-up may start
@@ -622,37 +599,29 @@ __global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid
         a.sched[1] = 0;
     }
     const uint32_t nqg = (a.q_heads + 7) / 8, nkg = (a.kv_heads + 3) / 4, groups = nqg + nkg;
-    const uint64_t units = static_cast<uint64_t>(a.B) * a.T * groups;
-    const uint64_t warps = static_cast<uint64_t>(gridDim.x) * (blockDim.x >> 5);
+    const uint32_t units = a.B * a.T * groups;  // below 2^31 (checked on the host)
+    const uint32_t warps = gridDim.x * (blockDim.x >> 5);
     const uint32_t d_lo = 4 * lane, d_hi = kD / 2 + 4 * lane;
-    for (uint64_t u = static_cast<uint64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); u < units;
-         u += warps) {
-        const uint64_t bt = u / groups;
-        const uint32_t grp = static_cast<uint32_t>(u % groups);
-        const uint32_t b = static_cast<uint32_t>(bt / a.T), t = static_cast<uint32_t>(bt % a.T);
+    for (uint32_t u = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < units; u += warps) {
+        const uint32_t bt = u / groups, grp = u - bt * groups;
+        const uint32_t b = bt / a.T, t = bt - b * a.T;
         const bool is_q = grp < nqg;
         const uint32_t h0 = is_q ? grp * 8 : (grp - nqg) * 4;
         const uint32_t n = is_q ? min(8u, a.q_heads - h0) : min(4u, a.kv_heads - h0);
+        // row i: q head h0+i, or k head h0+i (i < 4) / v head h0+i-4 (i >= 4)
         uint2 raw[8][2];
-        if (is_q) {
-            const uint16_t *src = a.q_raw + (bt * a.q_heads + h0) * kD;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (static_cast<uint32_t>(i) < n) {
-                    raw[i][0] = *reinterpret_cast<const uint2 *>(src + i * kD + d_lo);
-                    raw[i][1] = *reinterpret_cast<const uint2 *>(src + i * kD + d_hi);
-                }
-        } else {
-            const uint16_t *ks = a.k_raw + (bt * a.kv_heads + h0) * kD;
-            const uint16_t *vs = a.v_raw + (bt * a.kv_heads + h0) * kD;
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-                if (static_cast<uint32_t>(i) < n) {
-                    raw[i][0] = *reinterpret_cast<const uint2 *>(ks + i * kD + d_lo);
-                    raw[i][1] = *reinterpret_cast<const uint2 *>(ks + i * kD + d_hi);
-                    raw[4 + i][0] = *reinterpret_cast<const uint2 *>(vs + i * kD + d_lo);
-                    raw[4 + i][1] = *reinterpret_cast<const uint2 *>(vs + i * kD + d_hi);
-                }
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t hi_ = is_q ? static_cast<uint32_t>(i) : static_cast<uint32_t>(i & 3);
+            if (hi_ < n) {
+                const uint16_t *src =
+                    is_q ? a.q_raw + (static_cast<uint64_t>(bt) * a.q_heads + h0 + hi_) * kD
+                         : (i < 4 ? a.k_raw : a.v_raw) + (static_cast<uint64_t>(bt) * a.kv_heads + h0 + hi_) * kD;
+                raw[i][0] = *reinterpret_cast<const uint2 *>(src + d_lo);
+                raw[i][1] = *reinterpret_cast<const uint2 *>(src + d_hi);
+            } else {
+                raw[i][0] = raw[i][1] = make_uint2(0u, 0u);
+            }
         }
         const float pos = static_cast<float>(a.pos0 + t);
         float cs[4], sn[4], w[8];
@@ -664,35 +633,46 @@ __global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid
             w[e] = wsrc ? __uint_as_float(static_cast<uint32_t>(wsrc[d_lo + e]) << 16) : 1.0f;
             w[4 + e] = wsrc ? __uint_as_float(static_cast<uint32_t>(wsrc[d_hi + e]) << 16) : 1.0f;
         }
-        if (is_q) {
+        float lo[8][4], hi[8][4], ss[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                if (static_cast<uint32_t>(i) >= n) break;
-                float lo[4], hi[4];
-                unpack4(raw[i][0], lo);
-                unpack4(raw[i][1], hi);
-                norm_rope_pairs(lo, hi, a.qk_norm, w, a.eps, d_lo, a.rope_pairs, cs, sn);
-                uint16_t *dst = a.q_ws + ((static_cast<uint64_t>(b) * a.q_heads + h0 + i) * a.T + t) * kD;
-                *reinterpret_cast<uint2 *>(dst + d_lo) = pack4(lo);
-                *reinterpret_cast<uint2 *>(dst + d_hi) = pack4(hi);
+        for (int i = 0; i < 8; ++i) {
+            unpack4(raw[i][0], lo[i]);
+            unpack4(raw[i][1], hi[i]);
+            ss[i] = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) ss[i] += lo[i][e] * lo[i][e] + hi[i][e] * hi[i][e];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ss[i] += __shfl_xor_sync(0xffffffffu, ss[i], o);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const bool is_v = !is_q && i >= 4;
+            const bool norm = is_v ? a.v_norm != 0 : a.qk_norm != 0;
+            const float inv = norm ? rsqrtf(ss[i] * (1.0f / kD) + a.eps) : 1.0f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                lo[i][e] *= inv * (is_v ? 1.0f : w[e]);
+                hi[i][e] *= inv * (is_v ? 1.0f : w[4 + e]);
             }
-        } else {
-            const float ones[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+            if (!is_v) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                if (static_cast<uint32_t>(i) >= n) break;
-                const uint64_t off = ((static_cast<uint64_t>(b) * a.kv_heads + h0 + i) * a.capacity + a.pos0 + t) * kD;
-                float klo[4], khi[4], vlo[4], vhi[4];
-                unpack4(raw[i][0], klo);
-                unpack4(raw[i][1], khi);
-                unpack4(raw[4 + i][0], vlo);
-                unpack4(raw[4 + i][1], vhi);
-                norm_rope_pairs(klo, khi, a.qk_norm, w, a.eps, d_lo, a.rope_pairs, cs, sn);
-                norm_rope_pairs(vlo, vhi, a.v_norm, ones, a.eps, 0, 0, cs, sn);
-                *reinterpret_cast<uint2 *>(a.k_cache + off + d_lo) = pack4(klo);
-                *reinterpret_cast<uint2 *>(a.k_cache + off + d_hi) = pack4(khi);
-                *reinterpret_cast<uint2 *>(a.v_cache + off + d_lo) = pack4(vlo);
-                *reinterpret_cast<uint2 *>(a.v_cache + off + d_hi) = pack4(vhi);
+                for (int e = 0; e < 4; ++e)
+                    if (d_lo + e < a.rope_pairs) {
+                        const float l = lo[i][e], h = hi[i][e];
+                        lo[i][e] = l * cs[e] - h * sn[e];
+                        hi[i][e] = h * cs[e] + l * sn[e];
+                    }
+            }
+            const uint32_t hi_ = is_q ? static_cast<uint32_t>(i) : static_cast<uint32_t>(i & 3);
+            if (hi_ < n) {
+                uint16_t *dst =
+                    is_q ? a.q_ws + ((static_cast<uint64_t>(b) * a.q_heads + h0 + hi_) * a.T + t) * kD
+                         : (i < 4 ? a.k_cache : a.v_cache) +
+                               ((static_cast<uint64_t>(b) * a.kv_heads + h0 + hi_) * a.capacity + a.pos0 + t) * kD;
+                *reinterpret_cast<uint2 *>(dst + d_lo) = pack4(lo[i]);
+                *reinterpret_cast<uint2 *>(dst + d_hi) = pack4(hi[i]);
             }
         }
     }
@@ -731,6 +711,8 @@ int validate_prefill(const apex_attn_params *p, uint32_t capacity, uint32_t batc
         return fail(APEX_ERR_INVALID_ARGUMENT, n + ": pos0 + tokens exceeds capacity");
     const uint64_t items = static_cast<uint64_t>(batch) * p->q_heads * ((tokens + kBM - 1) / kBM);
     if (items > 0x7fffffffull) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": problem too large for one launch");
+    const uint64_t prep_units = static_cast<uint64_t>(batch) * tokens * ((p->q_heads + 7) / 8 + (p->kv_heads + 3) / 4);
+    if (prep_units > 0x7fffffffull) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": problem too large for one launch");
     const size_t need = ws_bytes(batch, tokens, p->q_heads);
     if (!workspace || workspace_bytes < need)
         return fail(APEX_ERR_WORKSPACE, n + ": workspace of " + std::to_string(need) + " bytes required");

@@ -15,8 +15,9 @@ sets (more bytes than the 126 MB L2 between reuses), bracketed by barrier + sync
 events on the launching stream, max over ranks.  The dominant kernel's own duration is taken
 with events around each of its launches (launches queued behind a GPU sleep so the events
 bracket only GPU work).  SM clocks and throttle reasons are sampled through NVML during the
-timed region.  N > 1: c2 / c1 run one replica per GPU (weak scaling), c3 shards sequences
-over GPUs, c5 splits the KV sequence over GPUs with one NCCL all-gather per step.
+timed region.  N > 1: c2 / c1 run one replica per GPU (weak scaling); c3 shards sequences, c4
+shards kv heads, c5 splits the KV sequence over GPUs with one NCCL all-gather per step (strong
+scaling: the total work is the configuration's).
 
 --impl reference times the reference's own CPU implementation of the path (oracle/_ref: the
 reference's cpu_ref.h + docs/B6_3_attention.md CPU functions) on the host cores, rank 0 only.
@@ -117,13 +118,20 @@ class ClockSampler(threading.Thread):
 # ---------------------------------------------------------------------------- workloads
 
 class PrefillWorkload:
-    """One fused prefill (prep + tcgen05 attention) per step over rotating input sets."""
+    """One fused prefill (prep + tcgen05 attention) per step over rotating input sets.  At N > 1,
+    c4 shards its kv heads (with their q heads) over the GPUs, no collective; c2 runs replicas."""
     kind = "prefill"
 
-    def __init__(self, cfg, device, seed):
+    def __init__(self, cfg, device, seed, rank=0, world=1):
+        import dataclasses
         import torch
         from apex_b200 import ops
         self.cfg, self.ops, self.torch = cfg, ops, torch
+        self.head_shard = cfg.name.startswith("c4") and world > 1
+        if self.head_shard:
+            if cfg.kv_heads % world:
+                raise SystemExit(f"{cfg.name}: {cfg.kv_heads} kv heads do not split over {world} GPUs")
+            cfg = dataclasses.replace(cfg, q_heads=cfg.q_heads // world, kv_heads=cfg.kv_heads // world)
         B, T, Hq, Hkv, D = cfg.batch, cfg.chunk, cfg.q_heads, cfg.kv_heads, cfg.head_dim
         self.B, self.T = B, T
         self.pos0 = cfg.seq_len - cfg.chunk            # the last chunk (the whole prompt for c2)
@@ -147,10 +155,10 @@ class PrefillWorkload:
             s["cache"] = ops.KvCache(s["kc"], s["vc"])
             self.sets.append(s)
         self.ws = ops.PrefillWorkspace(self.shape, B, T, device=device)
-        self.flops = prefill_flops(cfg, self.pos0, T) * B
-        self.tokens = B * T
+        self.flops = prefill_flops(cfg, self.pos0, T) * B      # this rank's heads
+        self.tokens = B * T if not self.head_shard or rank == 0 else 0
         self.launches_per_step = 2
-        self.kernel_name = "prefill_tc_kernel"
+        self.kernel_name = "prefill_pair_kernel"
 
     def step(self, i):
         s = self.sets[i % self.R]
@@ -427,7 +435,7 @@ def run_ours(args, cfg):
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
 
-    wl = (PrefillWorkload(cfg, device, cfg.seed * 1000 + rank) if cfg.kind == "prefill"
+    wl = (PrefillWorkload(cfg, device, cfg.seed * 1000 + rank, rank, world) if cfg.kind == "prefill"
           else DecodeWorkload(cfg, device, cfg.seed * 1000, rank, world))
     stream = torch.cuda.current_stream()
 
@@ -562,10 +570,12 @@ def run_ours(args, cfg):
     if rank != 0:
         return 0
     sharding = ("kv-split + all-gather" if getattr(wl, "kv_split", False)
-                else "batch-shard" if (cfg.lens_range and world > 1) else "replica")
+                else "batch-shard" if (cfg.lens_range and world > 1)
+                else "head-shard" if getattr(wl, "head_shard", False) else "replica")
     line = {
         "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": K, "warmup": args.warmup,
-        "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms_max / K, "higher_is_better": True,
+        "scaling": "weak" if sharding == "replica" else "strong", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (seeded randn on device)",
         "config": dict(config_of(cfg, args), parallelism=f"{sharding} x{world}",
                        l2=f"{wl.R} rotating input sets ({'graph replay' if use_graph else 'stream'}), "
