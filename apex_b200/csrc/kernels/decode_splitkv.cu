@@ -257,34 +257,42 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
     }
 
     // -------------------------------------------------------------------- consumers
-    // cos/sin of the new position, one pair per consumer thread: the per-row code below stays
-    // small (these short-lived CTAs run it once, so its instruction fetch is on the critical path)
+    // This warp's row (q of head kvh*G + warp for warps 0..G-1; the new k / v for warps G, G+1 of
+    // the split that owns the new position) and its norm weights are loaded first, so their latency
+    // overlaps the cos/sin table below.
+    const bool row_q = warp < kG, row_kv = !row_q && has_new, is_k = warp == kG;
+    uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+    float wv[8];
+    {
+        const uint16_t *src = row_q ? a.q_raw + (static_cast<uint64_t>(b) * Hq + kvh * kG + warp) * kD
+                                    : (is_k ? a.k_new : a.v_new) + (static_cast<uint64_t>(b) * a.kv_heads + kvh) * kD;
+        const uint16_t *w = row_q ? a.q_w : (is_k ? a.k_w : nullptr);
+        if (row_q || row_kv) raw = *reinterpret_cast<const uint4 *>(src + 8 * lane);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            wv[e] = w && (row_q || row_kv) ? __uint_as_float(static_cast<uint32_t>(w[8 * lane + e]) << 16) : 1.0f;
+    }
+    // cos/sin of the new position, one pair per consumer thread
     const float pos_f = static_cast<float>(pos_new);
     for (uint32_t i = tid; i < a.rope_pairs; i += kConsumerWarps * 32)
         rope_sincos(pos_f * a.rope.inv_freq[i], sm.rope_sn[i], sm.rope_cs[i]);
     consumer_sync();
-    if (warp < kG) {
-        // q of head kvh*G + warp: norm + rope at the new position, pre-scaled for exp2.
-        const uint32_t h = kvh * kG + warp;
-        const uint4 raw = *reinterpret_cast<const uint4 *>(
-            a.q_raw + (static_cast<uint64_t>(b) * Hq + h) * kD + 8 * lane);
+    if (row_q) {
+        // q: norm + rope at the new position, pre-scaled for exp2
         float x[8];
         unpack8(raw, x);
-        norm_rope_row_tab(x, lane, a.qk_norm, a.q_w, a.eps, a.rope_pairs, sm.rope_cs, sm.rope_sn);
+        norm_rope_row_tab(x, lane, a.qk_norm, wv, a.eps, a.rope_pairs, sm.rope_cs, sm.rope_sn);
 #pragma unroll
         for (int e = 0; e < 8; ++e) sm.q[warp][8 * lane + e] = x[e] * a.scale_log2;
-    } else if (has_new) {
-        // new k (warp 2): norm + rope; new v (warp 3): optional weightless norm.  Both are
-        // rounded to bf16 once, stored to the cache and kept in shared memory for this split.
-        const bool is_k = warp == kG;
-        const uint16_t *src = (is_k ? a.k_new : a.v_new) + (static_cast<uint64_t>(b) * a.kv_heads + kvh) * kD;
-        const uint4 raw = *reinterpret_cast<const uint4 *>(src + 8 * lane);
+    } else if (row_kv) {
+        // new k: norm + rope; new v: optional weightless norm.  Both are rounded to bf16 once, stored
+        // to the cache and kept in shared memory for this split.
         float x[8];
         unpack8(raw, x);
         if (is_k)
-            norm_rope_row_tab(x, lane, a.qk_norm, a.k_w, a.eps, a.rope_pairs, sm.rope_cs, sm.rope_sn);
+            norm_rope_row_tab(x, lane, a.qk_norm, wv, a.eps, a.rope_pairs, sm.rope_cs, sm.rope_sn);
         else
-            norm_rope_row_tab(x, lane, a.v_norm, nullptr, a.eps, 0, sm.rope_cs, sm.rope_sn);
+            norm_rope_row_tab(x, lane, a.v_norm, wv, a.eps, 0, sm.rope_cs, sm.rope_sn);
         const uint4 packed = pack8(x);
         *reinterpret_cast<uint4 *>((is_k ? sm.new_k : sm.new_v) + 8 * lane) = packed;
         uint16_t *dst = (is_k ? a.k_cache : a.v_cache) + head_base +

@@ -24,10 +24,10 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
     return v;
 }
 
-// RMSNorm (optional; weight bf16 `w`, or 1 when null) and RoPE of one 256-wide row held 8 dims per
-// lane; pair (i, i + 128) meets across lanes l and l ^ 16.  cos/sin of every pair come from tables
-// (cs[i], sn[i] for i < rope_pairs) computed beforehand.
-__device__ __forceinline__ void norm_rope_row_tab(float (&x)[8], uint32_t lane, bool norm, const uint16_t *w,
+// RMSNorm (optional; this lane's 8 weights `w`, already loaded) and RoPE of one 256-wide row held 8
+// dims per lane; pair (i, i + 128) meets across lanes l and l ^ 16.  cos/sin of every pair come from
+// tables (cs[i], sn[i] for i < rope_pairs) computed beforehand.
+__device__ __forceinline__ void norm_rope_row_tab(float (&x)[8], uint32_t lane, bool norm, const float (&w)[8],
                                                   float eps, uint32_t rope_pairs, const float *cs, const float *sn) {
     if (norm) {
         float ss = 0.f;
@@ -35,15 +35,9 @@ __device__ __forceinline__ void norm_rope_row_tab(float (&x)[8], uint32_t lane, 
         for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float inv = 1.0f / sqrtf(ss / static_cast<float>(kRowDim) + eps);
-        if (w) {  // element loads: the weight may sit at any even offset of a weights buffer
+        const float inv = rsqrtf(ss * (1.0f / static_cast<float>(kRowDim)) + eps);
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-                x[e] = x[e] * inv * __uint_as_float(static_cast<uint32_t>(w[8 * lane + e]) << 16);
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x[e] = x[e] * inv;
-        }
+        for (int e = 0; e < 8; ++e) x[e] = x[e] * inv * w[e];
     }
     if (rope_pairs) {
         const bool low = lane < 16;
