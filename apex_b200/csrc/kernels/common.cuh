@@ -117,6 +117,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
     }
     return true;
 }
+// Same contract as mbar_wait, for a thread that issues tcgen05.mma: polls with the non-blocking
+// test_wait and reads the clock only every 1024 polls.  On B200 a try_wait or a clock read on the
+// issuing thread costs about 90 cycles each, during which the tensor pipe runs dry, even when the
+// phase has already completed; a test_wait does not stall it.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, unsigned *status) {
+    if (mbar_test_wait(bar, parity)) return true;
+    long long start = 0;
+    for (uint32_t k = 1;; ++k) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((k & 1023u) == 0) {
+            const long long now = clock64();
+            if (start == 0) {
+                start = now;
+            } else if (now - start > kWaitBudgetCycles) {
+                atomicOr(status, kStatusTimeout);
+                return false;
+            }
+        }
+    }
+}
 
 // ------------------------------------------------------------------ TMA
 // 1-D bulk copy global -> shared, completion counted in bytes on `bar`.  src, dst 16-byte
@@ -348,27 +368,35 @@ __device__ __forceinline__ void tmem_relinquish_pair() {
 __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
 }
+// Pair MMAs and commits are called by all 32 lanes of a converged warp and issued by the lane
+// that elect.sync picks (the same lane every time, so a commit tracks that lane's MMAs).  The warp
+// computes the descriptors together: values it holds uniformly stay in uniform registers, which
+// keeps the issue loop short enough to feed 64-cycle MMAs back to back.
 __device__ __forceinline__ void tc_mma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                                uint32_t accumulate) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred p, e;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 __device__ __forceinline__ void tc_mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                                uint32_t accumulate) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred p, e;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 // Arrive once on the mbarrier at offset `bar` in both CTAs of the pair when all previously
-// issued pair MMAs of this thread complete.
+// issued pair MMAs of the elected lane complete.
 __device__ __forceinline__ void tc_commit_pair_both(uint32_t bar) {
     asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(bar),
         "h"(static_cast<uint16_t>(3))
         : "memory");
 }

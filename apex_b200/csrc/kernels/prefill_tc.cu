@@ -25,8 +25,10 @@
 //               slots in consumption order K(0) K(1) V(0) K(2) V(1) ...; all copies of the pair
 //               complete on CTA 0's barriers; tensor maps end at pos0+T (keys past the valid
 //               cache read as zeros).
-//       warp 1  TMEM owner (512 columns, allocated for the pair); in CTA 0, the MMA issuer.
-//               S_{t+1} is issued before PV_t.
+//       warp 1  TMEM owner (512 columns, allocated for the pair); in CTA 0, the MMA issuer: the
+//               whole warp runs the issue loop and one elected lane issues, so the descriptors
+//               stay in uniform registers and 64-cycle MMAs go back to back.  S_{t+1} is issued
+//               before PV_t.
 //       warps 4-11  two warpgroups per 128 query rows (TMEM lane = row; half 0 takes keys
 //               0-63 of each tile and dims 0-127, half 1 keys 64-127 and dims 128-255): online
 //               softmax in the log2 domain (mask only on tiles crossing the causal/window
@@ -286,7 +288,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (CTA 0)
-        if (leader && lane == 0) {
+        // The whole warp runs the loop (its values stay warp-uniform) and one elected lane issues
+        // each tcgen05 instruction; the waits poll with test_wait (mbar_wait_spin).
+        if (leader) {
+            auto wait_all = [&](uint32_t b, uint32_t parity) {
+                return __all_sync(0xffffffffu, mbar_wait_spin(b, parity, a.status));
+            };
             constexpr uint32_t idS = idesc_bf16_f32(2 * kBM, kBN, 0, 0);
             constexpr uint32_t idPV = idesc_bf16_f32(2 * kBM, kD, 0, 1);
             // Descriptors of the first K-step; every other step is a byte offset added to the
@@ -295,18 +302,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint64_t k_desc = smem_desc_sw128(sb + kOffSlots, 16, 1024);
             const uint64_t v_desc = smem_desc_sw128(sb + kOffSlots, kChunk, 1024);
             uint32_t gt = 0, n = 0;
-            auto wait_full = [&](uint32_t m) {
-                return mbar_wait(bar(kBarFull + m % kSlots), (m / kSlots) & 1, a.status);
-            };
+            auto wait_full = [&](uint32_t m) { return wait_all(bar(kBarFull + m % kSlots), (m / kSlots) & 1); };
             // O += P_t V_t; V(t) is the next two ring slots (keys [0,64) and [64,128)); P_t in TMEM
             // over S buffer t%2: keys [0,64) (softmax half 0) in columns [0,32), keys [64,128)
             // (half 1) in [64,96).  Each half's keys go as soon as that half has written P.
             auto issue_pv = [&](uint32_t t, bool first, uint32_t it) {
                 if (!alive) return;
-                if (first && it >= 1) alive = mbar_wait(bar(kBarOFree), (it - 1) & 1, a.status);
+                if (first && it >= 1) alive = wait_all(bar(kBarOFree), (it - 1) & 1);
                 const uint32_t p_col = tmem + kColS + (t & 1) * kBN;
                 for (int s = 0; s < 2 && alive; ++s) {
-                    if (!mbar_wait(bar(kBarP + 2 * s + (t & 1)), (t >> 1) & 1, a.status)) {
+                    if (!wait_all(bar(kBarP + 2 * s + (t & 1)), (t >> 1) & 1)) {
                         alive = false;
                         return;
                     }
@@ -327,11 +332,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 tc_commit_pair_both(bar(kBarO + (t & 1)));
             };
             for (uint32_t it = 0; alive; ++it) {
-                if (!mbar_wait(bar(kBarItem + it % kItemRing), (it / kItemRing) & 1, a.status)) break;
+                if (!wait_all(bar(kBarItem + it % kItemRing), (it / kItemRing) & 1)) break;
                 const int idx = items[it % kItemRing];
                 if (idx < 0) break;
                 const Item g = item_geometry(static_cast<uint32_t>(idx), a, 0);
-                if (!mbar_wait(bar(kBarQFull), it & 1, a.status)) break;
+                if (!wait_all(bar(kBarQFull), it & 1)) break;
                 tc_fence_after();
                 for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
                     const uint32_t t = gt + j;
