@@ -173,6 +173,8 @@ __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bul
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // Wait until this thread's committed bulk stores are complete.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// At most one committed bulk group of this thread may still be reading its shared-memory source.
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -287,6 +289,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 // ------------------------------------------------------------------ programmatic dependent launch
 // In a kernel launched with programmatic stream serialization: block until the preceding
 // kernel in the stream has completed and its memory is visible (a no-op otherwise).
+// Per-warpgroup register budget (all 128 threads of a warpgroup execute the same one).  inc waits
+// until other warpgroups have released enough registers: the block's split must not exceed the
+// registers it was launched with.
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Lets the next kernel in the stream (if launched with programmatic stream serialization) be
 // scheduled once every block of this grid has executed this or exited.

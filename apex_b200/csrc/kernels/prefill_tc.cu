@@ -55,34 +55,45 @@ constexpr uint32_t kSlotBytes = 2 * kChunk;          // 16 KB
 constexpr uint32_t kQBytes = kBM * kD * 2;           // 64 KB
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffSlots = kQBytes;
-constexpr uint32_t kOffStage = kOffSlots + kSlots * kSlotBytes;  // epilogue staging: 8 warps x [32 rows][64 B]
-constexpr uint32_t kStageWarpBytes = 32 * 64;
-constexpr uint32_t kOffBar = kOffStage + 8 * kStageWarpBytes;
+constexpr uint32_t kOffStage = kOffSlots + kSlots * kSlotBytes;  // epilogue staging: 4 warps x 2 x [32 rows][64 B]
+constexpr uint32_t kStageBytes = 32 * 64;
+constexpr uint32_t kStageWarpBytes = 2 * kStageBytes;
+constexpr uint32_t kOffBar = kOffStage + 4 * kStageWarpBytes;
 constexpr uint32_t kNumBars = 48;
 constexpr uint32_t kOffItems = kOffBar + 8 * kNumBars;
 constexpr uint32_t kItemRing = 8;
-constexpr uint32_t kOffRed = kOffItems + 4 * kItemRing;  // float [2 parity][2 half][128]
+constexpr uint32_t kOffRed = kOffItems + 4 * kItemRing;  // row sums, float [2 item parity][2 half][128]
 constexpr uint32_t kOffFlag = kOffRed + 2 * 2 * 128 * 4;
 constexpr uint32_t kOffTmem = kOffFlag + 16;
 constexpr uint32_t kSmemBytes = kOffTmem + 16;  // the dynamic shared memory base is 1024-aligned
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0, kColS = 256;
-constexpr int kThreads = 384;                        // 12 warps: 0 TMA, 1 TMEM/MMA, 4-11 softmax
+constexpr int kThreads = 512;                        // 16 warps: 0 TMA, 1 TMEM/MMA, 4-11 softmax, 12-15 epilogue
 constexpr float kTau = 8.0f;                         // lazy-rescale threshold (log2 units)
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr uint32_t kPairWarps = 16;                  // softmax warps of both CTAs
 constexpr uint32_t kHalfWarps = 8;                   // one softmax half of both CTAs
+constexpr uint32_t kSoftmaxThreads = 256;            // softmax threads of one CTA
+constexpr uint32_t kEpiThreads = 128;                // epilogue threads of one CTA
+constexpr uint32_t kEpiPairWarps = 8;                // epilogue warps of both CTAs
+// Registers per thread after setmaxnreg, per warpgroup (0: TMA + MMA, 1-2: softmax, 3: epilogue).
+// The launch gives each warpgroup 128 x 128; the split must add up to the same total.
+constexpr uint32_t kRegsTmaMma = 64, kRegsSoftmax = 168, kRegsEpilogue = 112;
+static_assert(kRegsTmaMma + 2 * kRegsSoftmax + kRegsEpilogue == 4 * (65536 / kThreads), "register split");
 
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 static_assert(kOffStage % 1024 == 0, "64-byte-swizzled staging tiles need 512-byte alignment");
 
 // barrier indices (8 bytes each at kOffBar).  CTA 0's copies of QFull, Full, P and OFree count
 // the pair; Empty, QEmpty, S and O are signalled in both CTAs by multicast commits.  P is one
-// barrier per (softmax half, tile parity), so PV can start on the first 64 keys early.
+// barrier per (softmax half, tile parity), so PV can start on the first 64 keys early.  L (row
+// sums written, by item parity) and LFree (row sums read) pass the row sums from the softmax
+// warps to the epilogue warps of the same CTA.  OItem completes once per item, when its last PV
+// is done: the epilogue waits on it rather than on O, whose phase may lag two behind.
 constexpr int kBarQFull = 0, kBarQEmpty = 1, kBarFull = 2, kBarEmpty = kBarFull + kSlots,
               kBarS = kBarEmpty + kSlots, kBarP = kBarS + 2, kBarO = kBarP + 4, kBarOFree = kBarO + 2,
-              kBarItem = kBarOFree + 1, kBarRed = kBarItem + kItemRing;
-static_assert(kBarRed + 2 <= kNumBars, "barrier budget");
+              kBarItem = kBarOFree + 1, kBarL = kBarItem + kItemRing, kBarLFree = kBarL + 2,
+              kBarOItem = kBarLFree + 2;
+static_assert(kBarOItem + 1 <= kNumBars, "barrier budget");
 
 struct PrefillArgs {
     uint16_t *out;        // [B][T][Hq][D]
@@ -120,6 +131,26 @@ __device__ __forceinline__ uint32_t visible_bits(int lo, int hi) {
     if (hi < lo) return 0u;
     const uint32_t upto_hi = hi == 31 ? 0xffffffffu : ((2u << hi) - 1u);
     return upto_hi & ~((1u << lo) - 1u);
+}
+
+// Masks one 32-key chunk of a warp's 32 rows (bit k of vis: key k visible in this lane's row).  The
+// masked band crosses a chunk in at most one warp of four, so the common cases are decided for the
+// whole warp at once.  Returns false when no row of the warp sees any key of the chunk (all -inf).
+__device__ __forceinline__ bool mask_chunk(uint32_t (&x)[32], uint32_t vis) {
+    if (__all_sync(0xffffffffu, vis == 0xffffffffu)) return true;
+    if (__all_sync(0xffffffffu, vis == 0u)) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) x[k] = 0xff800000u;  // -inf
+        return false;
+    }
+    // branch-free (a lane-dependent `if` per key costs the warp a divergent branch each): keep is
+    // all ones where key k is visible, and the rest becomes -inf
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+        const uint32_t keep = static_cast<uint32_t>(static_cast<int32_t>(vis << (31 - k)) >> 31);
+        x[k] = (x[k] & keep) | (0xff800000u & ~keep);
+    }
+    return true;
 }
 
 __device__ __forceinline__ Item item_geometry(uint32_t idx, const PrefillArgs &a, uint32_t rank) {
@@ -169,6 +200,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     volatile int *items = reinterpret_cast<volatile int *>(base + kOffItems);
     volatile uint32_t *err_flag = reinterpret_cast<volatile uint32_t *>(base + kOffFlag);
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(base + kOffTmem);
+    float *red = reinterpret_cast<float *>(base + kOffRed);  // row sums [2 item parity][2 half][128]
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t rank = cluster_rank();
@@ -185,9 +217,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar(kBarS + i), 1);
             mbar_init(bar(kBarO + i), 1);
-            mbar_init(bar(kBarRed + i), 2 * kBM);
+            mbar_init(bar(kBarL + i), kSoftmaxThreads);
+            mbar_init(bar(kBarLFree + i), kEpiThreads);
         }
-        mbar_init(bar(kBarOFree), kPairWarps);
+        mbar_init(bar(kBarOFree), kEpiPairWarps);
+        mbar_init(bar(kBarOItem), 1);
         for (uint32_t i = 0; i < kItemRing; ++i) mbar_init(bar(kBarItem + i), 1);
         *err_flag = 0;
         fence_mbar_init();
@@ -202,9 +236,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_holder;
     bool alive = true;
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer (+ scheduler in CTA 0)
-        if (lane == 0) {
+    // Both the TMA producer and the MMA issuer walk one stream of key tiles across items: K(t) /
+    // S(t) come before V(t-1) / PV(t-1) also when tile t opens the next item, so the next item's
+    // first scores are under way while the softmax still works on the previous item's last tile.
+    if (warp < 4) {
+        reg_dealloc<kRegsTmaMma>();
+        if (warp == 0 && lane == 0) {
+            // -------------------------------------------------------- TMA producer (+ scheduler in CTA 0)
             prefetch_tensormap(&tm_q);
             prefetch_tensormap(&tm_k);
             prefetch_tensormap(&tm_v);
@@ -223,11 +261,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 ++n;
                 return true;
             };
-            for (uint32_t it = 0;; ++it) {
+            // a box never starts past the cache end; the keys it then holds are masked
+            auto key_row = [&](uint32_t key) { return static_cast<int32_t>(min(key, a.kv_len - 1)); };
+            bool pend = false;  // V of the previous tile, loaded after the next tile's K
+            uint32_t pend_key = 0;
+            int32_t pend_row = 0;
+            auto load_v = [&]() {  // this CTA's 128 dims, keys [0,64) then [64,128)
+                for (int s = 0; s < 2 && alive; ++s) {
+                    uint32_t dst, full;
+                    if (!next_slot(dst, full)) {
+                        alive = false;
+                        break;
+                    }
+                    for (int c = 0; c < 2; ++c)
+                        tma_load_3d_pair(dst + c * kChunk, &tm_v, 128 * rank + 64 * c, key_row(pend_key + 64 * s),
+                                         pend_row, full);
+                }
+                pend = false;
+            };
+            for (uint32_t it = 0; alive; ++it) {
                 const uint32_t is = it % kItemRing;
                 int idx;
                 if (leader) {
-                    const uint32_t claimed = alive ? atomicAdd(a.sched, 1u) : a.n_items;
+                    const uint32_t claimed = atomicAdd(a.sched, 1u);
                     idx = claimed < a.n_items ? static_cast<int>(claimed) : -1;
                     items[is] = idx;
                     st_cluster_u32(mapa(sb + kOffItems + 4 * is, 1), static_cast<uint32_t>(idx));
@@ -243,54 +299,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (idx < 0) break;
                 const Item g = item_geometry(static_cast<uint32_t>(idx), a, rank);
                 const int32_t kv_row = static_cast<int32_t>(g.b * a.kv_heads + g.kvh);
-                // a box never starts past the cache end; the keys it then holds are masked
-                auto key_row = [&](uint32_t key) { return static_cast<int32_t>(min(key, a.kv_len - 1)); };
-                for (uint32_t j = 0; j <= g.n_tiles && alive; ++j) {
-                    if (j < g.n_tiles) {  // K(j): this CTA's 64 keys, dims [0,128) then [128,256)
-                        const uint32_t key = g.j_start + j * kBN + 64 * rank;
-                        for (int s = 0; s < 2 && alive; ++s) {
-                            uint32_t dst, full;
-                            if (!next_slot(dst, full)) {
-                                alive = false;
-                                break;
-                            }
-                            for (int c = 0; c < 2; ++c)
-                                tma_load_3d_pair(dst + c * kChunk, &tm_k, 128 * s + 64 * c, key_row(key), kv_row, full);
+                for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
+                    // K(j): this CTA's 64 keys, dims [0,128) then [128,256)
+                    const uint32_t key = g.j_start + j * kBN + 64 * rank;
+                    for (int s = 0; s < 2 && alive; ++s) {
+                        uint32_t dst, full;
+                        if (!next_slot(dst, full)) {
+                            alive = false;
+                            break;
                         }
-                        if (j == 0 && alive) {  // Q, once the previous item's S MMAs are done with it
-                            if (it >= 1 && !mbar_wait(bar(kBarQEmpty), (it - 1) & 1, a.status)) {
-                                alive = false;
-                                break;
-                            }
-                            if (leader) mbar_arrive_expect_tx(bar(kBarQFull), 2 * kQBytes);
-                            const uint32_t full = mapa(bar(kBarQFull), 0);
-                            for (int c = 0; c < 4; ++c)
-                                tma_load_3d_pair(sb + kOffQ + c * (kQBytes / 4), &tm_q, 64 * c,
-                                                 static_cast<int32_t>(g.q_row),
-                                                 static_cast<int32_t>(g.b * a.q_heads + g.h), full);
-                        }
+                        for (int c = 0; c < 2; ++c)
+                            tma_load_3d_pair(dst + c * kChunk, &tm_k, 128 * s + 64 * c, key_row(key), kv_row, full);
                     }
-                    if (j >= 1) {  // V(j-1): this CTA's 128 dims, keys [0,64) then [64,128)
-                        const uint32_t key = g.j_start + (j - 1) * kBN;
-                        for (int s = 0; s < 2 && alive; ++s) {
-                            uint32_t dst, full;
-                            if (!next_slot(dst, full)) {
-                                alive = false;
-                                break;
-                            }
-                            for (int c = 0; c < 2; ++c)
-                                tma_load_3d_pair(dst + c * kChunk, &tm_v, 128 * rank + 64 * c, key_row(key + 64 * s),
-                                                 kv_row, full);
+                    if (pend && alive) load_v();
+                    if (j == 0 && alive) {  // Q, once the previous item's S MMAs are done with it
+                        if (it >= 1 && !mbar_wait(bar(kBarQEmpty), (it - 1) & 1, a.status)) {
+                            alive = false;
+                            break;
                         }
+                        if (leader) mbar_arrive_expect_tx(bar(kBarQFull), 2 * kQBytes);
+                        const uint32_t full = mapa(bar(kBarQFull), 0);
+                        for (int c = 0; c < 4; ++c)
+                            tma_load_3d_pair(sb + kOffQ + c * (kQBytes / 4), &tm_q, 64 * c,
+                                             static_cast<int32_t>(g.q_row),
+                                             static_cast<int32_t>(g.b * a.q_heads + g.h), full);
                     }
+                    pend = true;
+                    pend_key = g.j_start + j * kBN;
+                    pend_row = kv_row;
                 }
             }
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer (CTA 0)
-        // The whole warp runs the loop (its values stay warp-uniform) and one elected lane issues
-        // each tcgen05 instruction; the waits poll with test_wait (mbar_wait_spin).
-        if (leader) {
+            if (pend && alive) load_v();
+        } else if (warp == 1 && leader) {
+            // -------------------------------------------------------- MMA issuer (CTA 0)
+            // The whole warp runs the loop (its values stay warp-uniform) and one elected lane issues
+            // each tcgen05 instruction; the waits poll with test_wait (mbar_wait_spin).
             auto wait_all = [&](uint32_t b, uint32_t parity) {
                 return __all_sync(0xffffffffu, mbar_wait_spin(b, parity, a.status));
             };
@@ -303,10 +346,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint64_t v_desc = smem_desc_sw128(sb + kOffSlots, kChunk, 1024);
             uint32_t gt = 0, n = 0;
             auto wait_full = [&](uint32_t m) { return wait_all(bar(kBarFull + m % kSlots), (m / kSlots) & 1); };
-            // O += P_t V_t; V(t) is the next two ring slots (keys [0,64) and [64,128)); P_t in TMEM
-            // over S buffer t%2: keys [0,64) (softmax half 0) in columns [0,32), keys [64,128)
-            // (half 1) in [64,96).  Each half's keys go as soon as that half has written P.
-            auto issue_pv = [&](uint32_t t, bool first, uint32_t it) {
+            auto issue_pv = [&](uint32_t t, bool first, bool last, uint32_t it) {
                 if (!alive) return;
                 if (first && it >= 1) alive = wait_all(bar(kBarOFree), (it - 1) & 1);
                 const uint32_t p_col = tmem + kColS + (t & 1) * kBN;
@@ -330,13 +370,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     ++n;
                 }
                 tc_commit_pair_both(bar(kBarO + (t & 1)));
+                if (last) tc_commit_pair_both(bar(kBarOItem));
             };
+            bool pend = false, pend_first = false, pend_last = false;  // PV of the previous tile, issued after the next S
+            uint32_t pend_t = 0, pend_it = 0;
             for (uint32_t it = 0; alive; ++it) {
-                if (!wait_all(bar(kBarItem + it % kItemRing), (it / kItemRing) & 1)) break;
+                if (!wait_all(bar(kBarItem + it % kItemRing), (it / kItemRing) & 1)) {
+                    alive = false;
+                    break;
+                }
                 const int idx = items[it % kItemRing];
                 if (idx < 0) break;
                 const Item g = item_geometry(static_cast<uint32_t>(idx), a, 0);
-                if (!wait_all(bar(kBarQFull), it & 1)) break;
+                if (!wait_all(bar(kBarQFull), it & 1)) {
+                    alive = false;
+                    break;
+                }
                 tc_fence_after();
                 for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
                     const uint32_t t = gt + j;
@@ -362,36 +411,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     if (!alive) break;
                     tc_commit_pair_both(bar(kBarS + (t & 1)));
                     if (j + 1 == g.n_tiles) tc_commit_pair_both(bar(kBarQEmpty));  // Q free once these finish
-                    if (j >= 1) issue_pv(t - 1, j - 1 == 0, it);
+                    if (pend) issue_pv(pend_t, pend_first, pend_last, pend_it);
+                    pend = true;
+                    pend_t = t;
+                    pend_first = j == 0;
+                    pend_last = j + 1 == g.n_tiles;
+                    pend_it = it;
                 }
-                issue_pv(gt + g.n_tiles - 1, g.n_tiles == 1, it);
                 gt += g.n_tiles;
             }
+            if (pend && alive) issue_pv(pend_t, pend_first, pend_last, pend_it);
         }
-    } else if (warp >= 4) {
-        // ------------------------------------------------------------ softmax + epilogue (both CTAs)
+    } else if (warp < 12) {
+        // ------------------------------------------------------------ softmax (both CTAs)
+        reg_alloc<kRegsSoftmax>();
         const uint32_t half = (warp - 4) >> 2, quad = warp & 3;
         const uint32_t r = quad * 32 + lane;                  // query row == TMEM lane
         const uint32_t lane_base = tmem + ((32u * quad) << 16);
         const uint32_t p_bar0 = mapa(bar(kBarP + 2 * half), 0), p_bar1 = mapa(bar(kBarP + 2 * half + 1), 0);
-        const uint32_t ofree_bar = mapa(bar(kBarOFree), 0);
-        float *red = reinterpret_cast<float *>(base + kOffRed);  // [2 parity][2 half][128]
-        uint32_t gt = 0, xchg = 0;
+        uint32_t gt = 0;
         // Wait for PV of global tile t.  o_done is a ring of two barriers indexed by tile parity:
         // when this runs (after S(t+1) or S(t) completed), PV(t-2) is already complete (it was
         // issued before those S MMAs) and PV(t+2) cannot have started, so the parity is
         // unambiguous without observing every phase.
         auto wait_pv = [&](uint32_t t) {
             alive = alive && __all_sync(0xffffffffu, mbar_wait(bar(kBarO + (t & 1)), (t >> 1) & 1, a.status));
-        };
-        auto exchange = [&](float mine, float &theirs) {
-            const uint32_t slot = xchg & 1;
-            red[(slot * 2 + half) * kBM + r] = mine;
-            mbar_arrive(bar(kBarRed + slot));
-            const bool ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarRed + slot), (xchg >> 1) & 1, a.status));
-            theirs = red[(slot * 2 + (half ^ 1)) * kBM + r];
-            ++xchg;
-            return ok;
         };
         // one elected lane per warp reports to CTA 0 after the warp's TMEM accesses are done
         auto warp_arrive = [&](uint32_t cluster_bar) {
@@ -439,19 +483,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         tmem_ld32(s_addr + 32 * c, sc);
                         tmem_ld32(o_addr + 32 * c, ov);
                         tc_wait_ld(sc, ov);
+                        bool sc_live = true, ov_live = true;
                         if (need_mask) {
-                            const uint32_t vo = visible_bits(lo - own - 32 * c, hi - own - 32 * c);
-                            const uint32_t vx = visible_bits(lo - oth - 32 * c, hi - oth - 32 * c);
-#pragma unroll
-                            for (int k = 0; k < 32; ++k) {
-                                if (!((vo >> k) & 1u)) sc[k] = 0xff800000u;  // -inf
-                                if (!((vx >> k) & 1u)) ov[k] = 0xff800000u;
-                            }
+                            sc_live = mask_chunk(sc, visible_bits(lo - own - 32 * c, hi - own - 32 * c));
+                            ov_live = mask_chunk(ov, visible_bits(lo - oth - 32 * c, hi - oth - 32 * c));
                         }
+                        if (ov_live) {
 #pragma unroll
-                        for (int k = 0; k < 32; k += 2) mx = fmax3(mx, __uint_as_float(ov[k]), __uint_as_float(ov[k + 1]));
+                            for (int k = 0; k < 32; k += 2) mx = fmax3(mx, __uint_as_float(ov[k]), __uint_as_float(ov[k + 1]));
+                        }
+                        if (sc_live) {
 #pragma unroll
-                        for (int k = 0; k < 32; k += 2) mx = fmax3(mx, __uint_as_float(sc[k]), __uint_as_float(sc[k + 1]));
+                            for (int k = 0; k < 32; k += 2) mx = fmax3(mx, __uint_as_float(sc[k]), __uint_as_float(sc[k + 1]));
+                        }
                     }
                 }
                 const float mt = mx * a.scale_log2;
@@ -496,28 +540,57 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 warp_arrive((tt & 1) ? p_bar1 : p_bar0);
             }
             if (!alive) break;
-            // epilogue: O / l -> bf16 out[b][t][h][half*128 ...]
-            wait_pv(gt + g.n_tiles - 1);
-            float l_other;
-            if (!exchange(l_part, l_other) || !alive) {
+            // this half's row sums go to the epilogue warps (slot it % 2, free once item it - 2's
+            // epilogue has read it)
+            if (it >= 2 && !__all_sync(0xffffffffu, mbar_wait(bar(kBarLFree + (it & 1)), ((it >> 1) - 1) & 1, a.status))) {
+                alive = false;
+                break;
+            }
+            red[((it & 1) * 2 + half) * kBM + r] = l_part;
+            mbar_arrive(bar(kBarL + (it & 1)));
+            gt += g.n_tiles;
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        // O / l -> bf16 out[b][t][h][...] for this CTA's 128 rows, once the item's last PV is done.
+        // Each 32-column chunk of a warp's 32 rows goes to global memory as one TMA store from a
+        // 2 KB staging tile ([32 rows][64 B], 64-byte swizzle: 16-byte piece q of row x at
+        // ((q ^ ((x >> 1) & 3)) * 16)), two tiles per warp in turn; rows at or past T are clipped by
+        // the tensor map.  O is released to the next item's PV once the last chunk is in registers.
+        reg_dealloc<kRegsEpilogue>();
+        const uint32_t quad = warp & 3;
+        const uint32_t r = quad * 32 + lane;
+        const uint32_t lane_base = tmem + ((32u * quad) << 16);
+        const uint32_t ofree_bar = mapa(bar(kBarOFree), 0);
+        uint8_t *stg = base + kOffStage + quad * kStageWarpBytes;
+        for (uint32_t it = 0; alive; ++it) {
+            if (!__all_sync(0xffffffffu, mbar_wait_cluster(bar(kBarItem + it % kItemRing), (it / kItemRing) & 1,
+                                                            a.status))) {
+                alive = false;
+                break;
+            }
+            const int idx = items[it % kItemRing];
+            if (idx < 0) break;
+            const Item g = item_geometry(static_cast<uint32_t>(idx), a, rank);
+            // the item's last PV (OItem completes once per item; the next item's PVs wait for this
+            // warp's O release, so the barrier cannot run a phase ahead)
+            if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarOItem), it & 1, a.status)) ||
+                !__all_sync(0xffffffffu, mbar_wait(bar(kBarL + (it & 1)), (it >> 1) & 1, a.status))) {
                 alive = false;
                 break;
             }
             tc_fence_after();
-            const float l_run = l_part + l_other;
+            const float l_run = red[((it & 1) * 2) * kBM + r] + red[((it & 1) * 2 + 1) * kBM + r];
+            mbar_arrive(bar(kBarLFree + (it & 1)));
             const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
-            // Each 32-column chunk of this warp's 32 rows goes to global memory as one TMA store
-            // from a 2 KB staging tile ([32 rows][64 B], 64-byte swizzle: 16-byte piece q of row x
-            // at ((q ^ ((x >> 1) & 3)) * 16)); rows at or past T are clipped by the tensor map.
-            uint8_t *stg = base + kOffStage + (warp - 4) * kStageWarpBytes;
             const bool any_rows = quad * 32 < g.rows_valid;
             uint32_t ob[2][32];  // chunk c is packed while chunk c + 1 is read from TMEM
-            tmem_ld32(lane_base + kColO + half * 128, ob[0]);
+            tmem_ld32(lane_base + kColO, ob[0]);
             tc_wait_ld(ob[0]);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 8; ++c) {
                 uint32_t(&o)[32] = ob[c & 1];
-                if (c < 3) tmem_ld32(lane_base + kColO + half * 128 + (c + 1) * 32, ob[(c + 1) & 1]);
+                if (c < 7) tmem_ld32(lane_base + kColO + (c + 1) * 32, ob[(c + 1) & 1]);
                 uint4 v[4];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -526,29 +599,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     v[q].z = pack_bf16(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
                     v[q].w = pack_bf16(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
                 }
-                if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging tile
+                uint8_t *buf = stg + (c & 1) * kStageBytes;
+                if (lane == 0) bulk_wait_read_1();  // the store that used this tile two chunks ago has read it
                 __syncwarp();
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                    *reinterpret_cast<uint4 *>(stg + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = v[q];
+                    *reinterpret_cast<uint4 *>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = v[q];
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0 && any_rows) {
-                    tma_store_4d(&tm_o, smem_u32(stg), static_cast<int32_t>(half * 128 + c * 32),
-                                 static_cast<int32_t>(g.h), static_cast<int32_t>(g.t0 + quad * 32),
-                                 static_cast<int32_t>(g.b));
+                    tma_store_4d(&tm_o, smem_u32(buf), static_cast<int32_t>(c * 32), static_cast<int32_t>(g.h),
+                                 static_cast<int32_t>(g.t0 + quad * 32), static_cast<int32_t>(g.b));
                     bulk_commit_group();
                 }
-                if (c < 3) tc_wait_ld(ob[(c + 1) & 1]);
+                if (c < 7) tc_wait_ld(ob[(c + 1) & 1]);
+                if (c == 6) {  // all of O is in registers: the next item's first PV may overwrite it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_remote(ofree_bar);
+                }
             }
-            warp_arrive(ofree_bar);
-            gt += g.n_tiles;
         }
+        if (lane == 0) bulk_wait_all();
     }
-    // Teardown.  The epilogue's TMA stores finish first.  After a failed wait, copies or MMAs of
-    // this pair may still be in flight: give them time to land (bounded) before the pair releases
-    // TMEM and shared memory.
-    if (warp >= 4 && lane == 0) bulk_wait_all();
+    // Teardown.  The epilogue's TMA stores have finished (above).  After a failed wait, copies or
+    // MMAs of this pair may still be in flight: give them time to land (bounded) before the pair
+    // releases TMEM and shared memory.
     if (!alive) *err_flag = 1u;
     __syncwarp();
     tc_fence_before();
