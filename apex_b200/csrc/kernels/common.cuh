@@ -23,6 +23,20 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
 }
+// bf16 pair (low half a * s, high half b * s), the two products in one packed f32x2 multiply
+// (sm_100) and both rounded to nearest even in one conversion.
+__device__ __forceinline__ uint32_t scale_pack_bf16(uint32_t a, uint32_t b, float s) {
+    uint32_t r;
+    asm("{\n\t.reg .b64 x, y, sc;\n\t.reg .b32 lo, hi;\n\t"
+        "mov.b64 x, {%1, %2};\n\t"
+        "mov.b64 sc, {%3, %3};\n\t"
+        "mul.rn.f32x2 y, x, sc;\n\t"
+        "mov.b64 {lo, hi}, y;\n\t"
+        "cvt.rn.bf16x2.f32 %0, hi, lo;\n\t}"
+        : "=r"(r)
+        : "r"(a), "r"(b), "r"(__float_as_uint(s)));
+    return r;
+}
 __device__ __forceinline__ float bf16_round(float x) {
     return __bfloat162float(__float2bfloat16_rn(x));
 }
@@ -117,25 +131,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
     }
     return true;
 }
-// Same contract as mbar_wait, for a thread that issues tcgen05.mma: polls with the non-blocking
-// test_wait and reads the clock only every 1024 polls.  On B200 a try_wait or a clock read on the
-// issuing thread costs about 90 cycles each, during which the tensor pipe runs dry, even when the
-// phase has already completed; a test_wait does not stall it.
+// Same contract as mbar_wait, for a thread that issues tcgen05.mma: checks first with the
+// non-blocking test_wait.  On B200 a try_wait or a clock read on the issuing thread costs about 90
+// cycles even when the phase has already completed, and the tensor pipe runs dry meanwhile; a
+// test_wait does not stall it.  A phase still open is waited for with try_wait, which suspends
+// the warp instead of taking issue slots from the warps that share its scheduler.
 __device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, unsigned *status) {
     if (mbar_test_wait(bar, parity)) return true;
-    long long start = 0;
-    for (uint32_t k = 1;; ++k) {
-        if (mbar_test_wait(bar, parity)) return true;
-        if ((k & 1023u) == 0) {
-            const long long now = clock64();
-            if (start == 0) {
-                start = now;
-            } else if (now - start > kWaitBudgetCycles) {
-                atomicOr(status, kStatusTimeout);
-                return false;
-            }
-        }
-    }
+    return mbar_wait(bar, parity, status);
 }
 
 // ------------------------------------------------------------------ TMA

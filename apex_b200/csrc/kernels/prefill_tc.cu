@@ -584,36 +584,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_arrive(bar(kBarLFree + (it & 1)));
             const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
             const bool any_rows = quad * 32 < g.rows_valid;
-            uint32_t ob[2][32];  // chunk c is packed while chunk c + 1 is read from TMEM
-            tmem_ld32(lane_base + kColO, ob[0]);
-            tc_wait_ld(ob[0]);
+            // 64 columns per TMEM load; each pair of 32-column chunks is packed to bf16 as soon as it
+            // lands, the next load is issued before the pair is staged, so a load is always in flight
+            uint32_t raw[64];
+            uint32_t(&raw_lo)[32] = *reinterpret_cast<uint32_t(*)[32]>(&raw[0]);
+            uint32_t(&raw_hi)[32] = *reinterpret_cast<uint32_t(*)[32]>(&raw[32]);
+            tmem_ld64(lane_base + kColO, raw);
+            tc_wait_ld(raw_lo, raw_hi);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint32_t(&o)[32] = ob[c & 1];
-                if (c < 7) tmem_ld32(lane_base + kColO + (c + 1) * 32, ob[(c + 1) & 1]);
-                uint4 v[4];
+            for (int pr = 0; pr < 4; ++pr) {
+                uint32_t pk[32];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    v[q].x = pack_bf16(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l);
-                    v[q].y = pack_bf16(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l);
-                    v[q].z = pack_bf16(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
-                    v[q].w = pack_bf16(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
-                }
-                uint8_t *buf = stg + (c & 1) * kStageBytes;
-                if (lane == 0) bulk_wait_read_1();  // the store that used this tile two chunks ago has read it
+                for (int i = 0; i < 32; ++i) pk[i] = scale_pack_bf16(raw[2 * i], raw[2 * i + 1], inv_l);
+                if (pr < 3) tmem_ld64(lane_base + kColO + 64 * (pr + 1), raw);
+                if (lane == 0) bulk_wait_read_all();  // the previous pair's stores have read both tiles
                 __syncwarp();
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    *reinterpret_cast<uint4 *>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = v[q];
+                for (int h = 0; h < 2; ++h) {
+                    uint8_t *buf = stg + h * kStageBytes;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        *reinterpret_cast<uint4 *>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) =
+                            make_uint4(pk[16 * h + 4 * q], pk[16 * h + 4 * q + 1], pk[16 * h + 4 * q + 2],
+                                       pk[16 * h + 4 * q + 3]);
+                }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0 && any_rows) {
-                    tma_store_4d(&tm_o, smem_u32(buf), static_cast<int32_t>(c * 32), static_cast<int32_t>(g.h),
-                                 static_cast<int32_t>(g.t0 + quad * 32), static_cast<int32_t>(g.b));
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                        tma_store_4d(&tm_o, smem_u32(stg + h * kStageBytes), static_cast<int32_t>(64 * pr + 32 * h),
+                                     static_cast<int32_t>(g.h), static_cast<int32_t>(g.t0 + quad * 32),
+                                     static_cast<int32_t>(g.b));
                     bulk_commit_group();
                 }
-                if (c < 7) tc_wait_ld(ob[(c + 1) & 1]);
-                if (c == 6) {  // all of O is in registers: the next item's first PV may overwrite it
+                if (pr < 3) tc_wait_ld(raw_lo, raw_hi);
+                if (pr == 2) {  // all of O is in registers: the next item's first PV may overwrite it
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive_remote(ofree_bar);
