@@ -76,6 +76,54 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
+// ------------------------------------------------------------------ packed f32x2 arithmetic (sm_100)
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f32x2_split(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t sub_f32x2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// 2^x0 and 2^x1 on the FMA pipe (x <= 8; x is clamped at -126, so -inf gives 2^-126 or a denormal,
+// never a wrapped exponent: the cubic's value is in [0.7, 1.5]), to take part of a softmax's
+// exponentials off the MUFU pipe.  Cody-Waite style reduction x = j + f, j = rint(x) by the
+// 1.5 * 2^23 shift, f in [-1/2, 1/2]; 2^f by a cubic whose coefficients are the least-squares fit
+// of 2^f on 2001 equally spaced points of [-1/2, 1/2] (maximum relative error 1.9e-4 over
+// [-30, 0], well below the 2^-9 of the bf16 P it feeds); 2^j is added to the exponent field.
+__device__ __forceinline__ void exp2_poly_x2(uint64_t x2, float &p0, float &p1) {
+    float x0, x1;
+    f32x2_split(x2, x0, x1);
+    const uint64_t x = f32x2(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+    const uint64_t shift = f32x2(12582912.0f, 12582912.0f);
+    const uint64_t t = add_f32x2(x, shift);
+    const uint64_t f = sub_f32x2(x, sub_f32x2(t, shift));
+    uint64_t q = fma_f32x2(f32x2(0.0558758713f, 0.0558758713f), f, f32x2(0.242296502f, 0.242296502f));
+    q = fma_f32x2(q, f, f32x2(0.693127215f, 0.693127215f));
+    q = fma_f32x2(q, f, f32x2(0.999948144f, 0.999948144f));
+    float q0, q1, t0, t1;
+    f32x2_split(q, q0, q1);
+    f32x2_split(t, t0, t1);
+    // unsigned: the shift moves j's low bits (two's complement) into the exponent field and wraps
+    p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+    p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
+}
+
 // ------------------------------------------------------------------ shared-memory addresses
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -507,16 +507,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     m_run = mt;
                 }
                 const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
-                float sum[4] = {0.f, 0.f, 0.f, 0.f};
+                // p = 2^(s * scale - m) in packed f32x2 arithmetic; 12 of the 64 exponentials run as a
+                // polynomial on the FMA pipe, the rest on MUFU (which alone would bound this loop)
+                uint64_t sum2[2] = {0ull, 0ull};
                 uint32_t packed[32];
+                const uint64_t scale2 = f32x2(a.scale_log2, a.scale_log2), neg_m2 = f32x2(neg_m, neg_m);
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    const float p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * i]), a.scale_log2, neg_m));
-                    const float p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * i + 1]), a.scale_log2, neg_m));
-                    sum[i & 3] += p0 + p1;
+                    const uint64_t x2 = fma_f32x2(f32x2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])),
+                                                  scale2, neg_m2);
+                    float p0, p1;
+                    if (i % 5 == 2 && i < 30) {
+                        exp2_poly_x2(x2, p0, p1);
+                    } else {
+                        float x0, x1;
+                        f32x2_split(x2, x0, x1);
+                        p0 = fast_exp2(x0);
+                        p1 = fast_exp2(x1);
+                    }
+                    sum2[i & 1] = add_f32x2(sum2[i & 1], f32x2(p0, p1));
                     packed[i] = pack_bf16(p0, p1);
                 }
-                l_part = l_part * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
+                float s0, s1, s2, s3;
+                f32x2_split(sum2[0], s0, s1);
+                f32x2_split(sum2[1], s2, s3);
+                l_part = l_part * alpha + ((s0 + s1) + (s2 + s3));
                 // tcgen05.ld/st are warp-collective: the whole warp rescales if any row must, after
                 // PV of the previous tile has finished accumulating into O.
                 if (__any_sync(0xffffffffu, rescale)) {
