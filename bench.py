@@ -45,11 +45,11 @@ L2_BYTES = 126 * 1024 * 1024
 # (profiles/*.md names the command); None until captured for that workload.
 NCU_TRAFFIC_BYTES = {
     # prefill_pair_kernel, --set full capture; the 16.8 MB output is still in L2 at kernel end
-    "c2_prefill_window": 33_618_688 + 107_520,
+    "c2_prefill_window": 33_634_816 + 313_856,
     # decode_splitkv_kernel, launch-list capture, mean over 66 launches
     "c3_ragged_decode": 2_307_200_000,
     # prefill_pair_kernel, --set full capture
-    "c4_chunked_prefill": 1_430_709_000 + 127_423_488,
+    "c4_chunked_prefill": 1_559_600_000 + 129_579_776,
     # decode_splitkv_kernel, --set full capture
     "c5_long_decode_b1": 1_078_009_000 + 11_022_336,
 }
