@@ -527,8 +527,10 @@ def run_ours(args, cfg):
     torch.cuda.synchronize()
     ops.device_status()
 
-    # graph of R steps (one per rotating set); K steps = whole replays + a partial tail graph
-    use_graph = not getattr(wl, "kv_split", False)
+    # graph of R steps (one per rotating set); K steps = whole replays + a partial tail graph.  The
+    # KV-split decode's NCCL all-gather is captured with the kernels.  Capturing is an optimisation
+    # of the host side only: if it fails on any rank, every rank runs the steps eagerly, so that all
+    # ranks take the same collectives.
     graphs = {}
 
     def graph_for(n):
@@ -541,12 +543,27 @@ def run_ours(args, cfg):
         return graphs[n]
 
     K = args.steps
-    if use_graph:
-        full, tail = divmod(K, wl.R)
+    full, tail = divmod(K, wl.R)
+    try:
         if full:
             graph_for(wl.R)
         if tail:
             graph_for(tail)
+        captured = 1
+    except Exception:
+        graphs.clear()
+        captured = 0
+    torch.cuda.synchronize()
+    if world > 1:
+        flag = torch.tensor([captured], dtype=torch.int32, device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        captured = int(flag.item())
+    if not captured:
+        graphs.clear()
+    use_graph = bool(captured)
+    if use_graph and world > 1:  # a warm replay of each graph before the timed region
+        for g in graphs.values():
+            g.replay()
         torch.cuda.synchronize()
 
     sampler = ClockSampler(local)
