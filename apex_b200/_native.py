@@ -27,6 +27,8 @@ EXPORTED = (
     "apex_attn_decode_workspace_init", "apex_attn_decode_bf16", "apex_attn_decode_partial_bf16",
     "apex_attn_merge_partials", "apex_attn_prefill_workspace_bytes", "apex_attn_prefill_bf16",
     "apex_attn_prefill_prep_bf16", "apex_attn_prefill_attend_bf16", "apex_attn_decode_bf16_noalloc",
+    "apex_attn_peer_exchange_bytes", "apex_attn_decode_kvsplit_bf16", "apex_device_alloc",
+    "apex_device_free", "apex_ipc_get_handle", "apex_ipc_open_handle", "apex_ipc_close_handle",
 )
 
 
@@ -45,9 +47,21 @@ class AttnParams(ctypes.Structure):
                 ("qk_norm", ctypes.c_uint32), ("v_norm", ctypes.c_uint32)]
 
 
+MAX_PEERS = 8
+
+
+class PeerExchange(ctypes.Structure):
+    """apex_peer_exchange (include/apex_cuda.h): every rank's exchange buffers as mapped here."""
+    _fields_ = [("rank", ctypes.c_uint32), ("world", ctypes.c_uint32),
+                ("gather", ctypes.c_void_p * MAX_PEERS), ("flags", ctypes.c_void_p * MAX_PEERS),
+                ("seq", ctypes.c_void_p)]
+
+
 _lib = None
 _vp, _u32, _f32, _sz, _i32 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_float, ctypes.c_size_t, ctypes.c_int
 _PP = ctypes.POINTER(AttnParams)
+_PX = ctypes.POINTER(PeerExchange)
+_PSZ = ctypes.POINTER(ctypes.c_size_t)
 
 
 def load(path: str | pathlib.Path | None = None):
@@ -74,6 +88,14 @@ def load(path: str | pathlib.Path | None = None):
     L.apex_attn_decode_partial_bf16.argtypes = ([_PP] + [_vp] * 7 + [_u32, _vp, _u32, _u32, _u32, _u32,
                                                                        _vp, _vp, _sz, _vp])
     L.apex_attn_merge_partials.argtypes = [_vp, _u32, _u32, _u32, _vp, _vp]
+    L.apex_attn_peer_exchange_bytes.argtypes = [_PP, _u32, _u32, _PSZ, _PSZ, _PSZ]
+    L.apex_attn_decode_kvsplit_bf16.argtypes = ([_PP] + [_vp] * 7 + [_u32, _vp, _u32, _u32, _u32, _u32, _PX,
+                                                                       _vp, _vp, _sz, _vp])
+    L.apex_device_alloc.argtypes = [_sz, ctypes.POINTER(_vp)]
+    L.apex_device_free.argtypes = [_vp]
+    L.apex_ipc_get_handle.argtypes = [_vp, _vp]
+    L.apex_ipc_open_handle.argtypes = [_vp, ctypes.POINTER(_vp)]
+    L.apex_ipc_close_handle.argtypes = [_vp]
     L.apex_attn_prefill_workspace_bytes.argtypes = [_PP, _u32, _u32]
     L.apex_attn_prefill_workspace_bytes.restype = _sz
     L.apex_attn_prefill_bf16.argtypes = ([_PP] + [_vp] * 7 + [_u32, _u32, _u32, _u32, _vp, _vp, _sz, _vp])

@@ -6,6 +6,8 @@
 #include <vector>
 
 #include "common.cuh"
+#include <cstring>
+
 #include "internal.h"
 
 namespace apex {
@@ -159,6 +161,52 @@ int apex_cuda_device_status(void *stream) {
                           "a kernel skipped a sequence whose length exceeded max_seq_len or the cache");
     }
     return apex::ok();
+}
+
+int apex_device_alloc(size_t bytes, void **ptr) {
+    if (!ptr || bytes == 0) return apex::fail(APEX_ERR_INVALID_ARGUMENT, "apex_device_alloc: null pointer or size 0");
+    *ptr = nullptr;
+    int rc = apex::check_cuda(cudaMalloc(ptr, bytes), "apex_device_alloc");
+    if (rc) return rc;
+    rc = apex::check_cuda(cudaMemset(*ptr, 0, bytes), "apex_device_alloc: zero");
+    if (rc) {
+        cudaFree(*ptr);
+        *ptr = nullptr;
+        return rc;
+    }
+    return apex::ok();
+}
+
+int apex_device_free(void *ptr) {
+    if (!ptr) return apex::ok();
+    const int rc = apex::check_cuda(cudaFree(ptr), "apex_device_free");
+    return rc ? rc : apex::ok();
+}
+
+int apex_ipc_get_handle(const void *ptr, void *handle64) {
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+    if (!ptr || !handle64) return apex::fail(APEX_ERR_INVALID_ARGUMENT, "apex_ipc_get_handle: null pointer");
+    cudaIpcMemHandle_t h;
+    const int rc = apex::check_cuda(cudaIpcGetMemHandle(&h, const_cast<void *>(ptr)), "apex_ipc_get_handle");
+    if (rc) return rc;
+    memcpy(handle64, &h, sizeof(h));
+    return apex::ok();
+}
+
+int apex_ipc_open_handle(const void *handle64, void **ptr) {
+    if (!handle64 || !ptr) return apex::fail(APEX_ERR_INVALID_ARGUMENT, "apex_ipc_open_handle: null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    *ptr = nullptr;
+    const int rc = apex::check_cuda(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess),
+                                    "apex_ipc_open_handle");
+    return rc ? rc : apex::ok();
+}
+
+int apex_ipc_close_handle(void *ptr) {
+    if (!ptr) return apex::ok();
+    const int rc = apex::check_cuda(cudaIpcCloseMemHandle(ptr), "apex_ipc_close_handle");
+    return rc ? rc : apex::ok();
 }
 
 }  // extern "C"

@@ -43,6 +43,7 @@ constexpr int kPosPerWarp = kStagePos / kConsumerWarps;
 constexpr int kPart = kD + 2;           // public partial record: o[D], m, l
 constexpr int kWsRec = kD + 4;          // workspace record: o[D], m, l, pad (16-byte multiple)
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint32_t kMaxPeers = 8;       // GPUs of one NVLink domain that share a KV range
 
 struct DecodeArgs {
     const uint16_t *q_raw, *k_new, *v_new, *q_w, *k_w;
@@ -57,6 +58,14 @@ struct DecodeArgs {
     uint32_t chunk, max_splits, kv_begin, kv_end, max_seq_len;
     float rope_base, eps, scale_log2;
     int partial_mode;
+    // peer mode (a KV range split over `world` GPUs): this rank's partial goes straight into every
+    // rank's gather buffer over NVLink, a per-step sequence flag follows it, and the rank merges
+    // all partials itself once every rank's flag has arrived (no collective launch, no merge launch)
+    int peer_mode;
+    uint32_t rank, world;
+    float *peer_gather[kMaxPeers];    // rank r's [2 step parity][world][B*Hq][D+4] f32, mapped here
+    unsigned *peer_flags[kMaxPeers];  // rank r's [world][B*Hkv] last published step
+    unsigned *peer_seq;               // this rank's [B*Hkv] step counters
     RopeTable rope;      // inv_freq[i] = rope_base^(-2i/256)
 };
 
@@ -73,6 +82,14 @@ struct __align__(16) DecodeSmem {
     int is_last;
 };
 
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
 }
@@ -188,6 +205,76 @@ __device__ __forceinline__ void consumer_reduce(float (&v)[kG], float (&red)[kCo
         v[g] = r;
     }
     consumer_sync();
+}
+
+// Peer mode: publish this rank's partial of (b, kv head) -- thread t holds head g = t / 64, dims
+// [d0, d0+4) of the normalised o, and (m, l) when d0 = 0 -- to every rank, then merge all ranks'
+// partials into bf16 out.  Steps alternate between two gather slots, so a rank that runs ahead never
+// overwrites data a slower peer is still merging (it cannot start step k+2 before every peer has
+// published step k+1, which each peer does only after finishing step k).  The wait for the peers'
+// flags is bounded: on expiry the status word gets kStatusTimeout and the output is left unwritten.
+__device__ void peer_publish_merge(const DecodeArgs &a, DecodeSmem &sm, uint32_t b, uint32_t kvh, uint32_t tid,
+                                   uint32_t g, uint32_t d0, const float (&o)[4], float m, float l) {
+    const uint32_t bhkv = gridDim.z * a.kv_heads, bkv = b * a.kv_heads + kvh;
+    const uint64_t rows = static_cast<uint64_t>(gridDim.z) * a.q_heads;
+    const uint64_t row = static_cast<uint64_t>(b) * a.q_heads + kvh * kG + g;
+    const unsigned seq = *reinterpret_cast<volatile unsigned *>(a.peer_seq + bkv) + 1u;
+    const uint32_t par = seq & 1u;
+    for (uint32_t p = 0; p < a.world; ++p) {
+        float *dst = a.peer_gather[p] + ((static_cast<uint64_t>(par) * a.world + a.rank) * rows + row) * kWsRec;
+        *reinterpret_cast<float4 *>(dst + d0) = make_float4(o[0], o[1], o[2], o[3]);
+        if (d0 == 0) {
+            dst[kD] = m;
+            dst[kD + 1] = l;
+        }
+    }
+    consumer_sync();
+    if (tid == 0) {
+        a.peer_seq[bkv] = seq;
+        __threadfence_system();  // every thread's stores above (ordered by the barrier) before the flags
+        for (uint32_t p = 0; p < a.world; ++p) st_release_sys(a.peer_flags[p] + a.rank * bhkv + bkv, seq);
+        const unsigned *mine = a.peer_flags[a.rank] + bkv;
+        const long long start = clock64();
+        bool ok = true;
+        for (uint32_t r = 0; r < a.world && ok; ++r) {
+            while (static_cast<int>(ld_acquire_sys(mine + r * bhkv) - seq) < 0) {
+                if (clock64() - start > kWaitBudgetCycles) {
+                    atomicOr(a.status, kStatusTimeout);
+                    ok = false;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        sm.is_last = ok;
+    }
+    consumer_sync();
+    if (!sm.is_last) return;
+    // log-sum-exp merge over the ranks (each partial: o normalised by its l, l relative to its m)
+    const float *base = a.peer_gather[a.rank] + static_cast<uint64_t>(par) * a.world * rows * kWsRec;
+    float M = -INFINITY;
+    for (uint32_t r = 0; r < a.world; ++r) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(base + (r * rows + row) * kWsRec + kD));
+        if (ml.y > 0.f) M = fmaxf(M, ml.x);
+    }
+    float den = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (uint32_t r = 0; r < a.world; ++r) {
+        const float *src = base + (r * rows + row) * kWsRec;
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(src + kD));
+        if (!(ml.y > 0.f)) continue;
+        const float wt = fast_exp2(ml.x - M) * ml.y;
+        const float4 ov = __ldcg(reinterpret_cast<const float4 *>(src + d0));
+        den += wt;
+        acc[0] += wt * ov.x;
+        acc[1] += wt * ov.y;
+        acc[2] += wt * ov.z;
+        acc[3] += wt * ov.w;
+    }
+    const float inv = den > 0.f ? 1.0f / den : 0.f;
+    uint2 packed;
+    packed.x = pack_bf16(acc[0] * inv, acc[1] * inv);
+    packed.y = pack_bf16(acc[2] * inv, acc[3] * inv);
+    *reinterpret_cast<uint2 *>(a.out + row * kD + d0) = packed;
 }
 
 __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __grid_constant__ DecodeArgs a) {
@@ -373,7 +460,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
     const uint64_t row = static_cast<uint64_t>(b) * Hq + h;
 
     if (nsplit == 1) {
-        if (a.partial_mode) {
+        if (a.peer_mode) {
+            peer_publish_merge(a, sm, b, kvh, tid, g, d0, o, M, den);
+        } else if (a.partial_mode) {
             float *dst = a.partial_out + row * kPart;
 #pragma unroll
             for (int e = 0; e < 4; ++e) dst[d0 + e] = o[e];
@@ -468,7 +557,10 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
     }
     const float Mx = mx[g], dtot = dsum[g];
     const float inv = dtot > 0.f ? 1.0f / dtot : 0.f;
-    if (a.partial_mode) {
+    if (a.peer_mode) {
+        const float on[4] = {r[0] * inv, r[1] * inv, r[2] * inv, r[3] * inv};
+        peer_publish_merge(a, sm, b, kvh, tid, g, d0, on, Mx, dtot);
+    } else if (a.partial_mode) {
         // A rank partial stores l relative to its own max Mx: l_rank = sum_s 2^(m_s - Mx) l_s.
         float *dst = a.partial_out + row * kPart;
 #pragma unroll
@@ -563,14 +655,27 @@ int launch_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16
                   const int32_t *seq_lens, uint32_t batch, uint32_t max_seq_len,
                   uint32_t kv_begin, uint32_t kv_end, bool partial_mode, uint16_t *out,
                   float *partial_out, void *workspace, size_t workspace_bytes_given, void *stream,
-                  const char *name) {
+                  const char *name, const apex_peer_exchange *peer = nullptr) {
     int rc = check_params(p, name);
     if (rc) return rc;
     if (batch == 0) return ok();
     if (batch > 65535) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": batch > 65535");
     if (!q_raw || !k_new || !v_new || !k_cache || !v_cache || !seq_lens ||
-        (partial_mode ? !partial_out : !out))
+        (partial_mode && !peer ? !partial_out : !out))
         return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": null tensor");
+    if (peer) {
+        if (peer->world < 1 || peer->world > kMaxPeers || peer->rank >= peer->world)
+            return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": need 1 <= world <= 8 and rank < world");
+        if (!peer->seq) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": null step counters");
+        // one CTA per (sequence, kv head) waits for the other ranks while holding its SM slot; at
+        // most one per SM keeps every rank's remaining CTAs schedulable
+        if (static_cast<uint64_t>(batch) * p->kv_heads > static_cast<uint64_t>(sm_count()))
+            return fail(APEX_ERR_UNSUPPORTED, std::string(name) + ": batch * kv_heads above the SM count");
+        for (uint32_t r = 0; r < peer->world; ++r)
+            if (!peer->gather[r] || !peer->flags[r] || !aligned16(peer->gather[r]))
+                return fail(APEX_ERR_INVALID_ARGUMENT,
+                            std::string(name) + ": every rank's gather buffer (16-byte aligned) and flags are needed");
+    }
     for (const void *ptr : {(const void *)q_raw, (const void *)k_new, (const void *)v_new,
                             (const void *)k_cache, (const void *)v_cache})
         if (!aligned16(ptr)) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": tensors must be 16-byte aligned");
@@ -601,6 +706,16 @@ int launch_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16
     a.kv_begin = kv_begin; a.kv_end = kv_end; a.max_seq_len = max_seq_len;
     a.rope_base = p->rope_base; a.eps = p->eps; a.scale_log2 = p->scale * kLog2e;
     a.partial_mode = partial_mode ? 1 : 0;
+    if (peer) {
+        a.peer_mode = 1;
+        a.rank = peer->rank;
+        a.world = peer->world;
+        for (uint32_t r = 0; r < peer->world; ++r) {
+            a.peer_gather[r] = peer->gather[r];
+            a.peer_flags[r] = peer->flags[r];
+        }
+        a.peer_seq = peer->seq;
+    }
     rope_table(a.rope.inv_freq, p->rope_pairs, kD, p->rope_base);
     a.status = device_status_ptr();
     if (!a.status) return fail(APEX_ERR_CUDA, std::string(name) + ": device status word unavailable");
@@ -668,6 +783,35 @@ extern "C" int apex_attn_decode_partial_bf16(const apex_attn_params *p, const ui
                                capacity, seq_lens, batch, max_seq_len, kv_begin, kv_end, true,
                                nullptr, partial, workspace, workspace_bytes, stream,
                                "apex_attn_decode_partial_bf16");
+}
+
+extern "C" int apex_attn_peer_exchange_bytes(const apex_attn_params *p, uint32_t batch, uint32_t world,
+                                             size_t *gather_bytes, size_t *flag_bytes, size_t *seq_bytes) {
+    using namespace apex;
+    int rc = check_params(p, "apex_attn_peer_exchange_bytes");
+    if (rc) return rc;
+    if (world < 1 || world > kMaxPeers)
+        return fail(APEX_ERR_INVALID_ARGUMENT, "apex_attn_peer_exchange_bytes: need 1 <= world <= 8");
+    if (!gather_bytes || !flag_bytes || !seq_bytes)
+        return fail(APEX_ERR_INVALID_ARGUMENT, "apex_attn_peer_exchange_bytes: null output");
+    *gather_bytes = 2ull * world * batch * p->q_heads * kWsRec * sizeof(float);  // 16-byte records
+    *flag_bytes = static_cast<size_t>(world) * batch * p->kv_heads * sizeof(uint32_t);
+    *seq_bytes = static_cast<size_t>(batch) * p->kv_heads * sizeof(uint32_t);
+    return ok();
+}
+
+extern "C" int apex_attn_decode_kvsplit_bf16(const apex_attn_params *p, const uint16_t *q_raw,
+                                             const uint16_t *k_new, const uint16_t *v_new,
+                                             const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                                             uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
+                                             const int32_t *seq_lens, uint32_t batch, uint32_t max_seq_len,
+                                             uint32_t kv_begin, uint32_t kv_end, const apex_peer_exchange *x,
+                                             uint16_t *out, void *workspace, size_t workspace_bytes,
+                                             void *stream) {
+    if (!x) return apex::fail(APEX_ERR_INVALID_ARGUMENT, "apex_attn_decode_kvsplit_bf16: null peer exchange");
+    return apex::launch_decode(p, q_raw, k_new, v_new, q_norm_w, k_norm_w, k_cache, v_cache, capacity, seq_lens,
+                               batch, max_seq_len, kv_begin, kv_end, true, out, nullptr, workspace,
+                               workspace_bytes, stream, "apex_attn_decode_kvsplit_bf16", x);
 }
 
 extern "C" int apex_attn_merge_partials(const float *partials, uint32_t num_partials,

@@ -5,14 +5,18 @@ Only two shardings exist, where the work splits naturally:
 * batch sharding (ragged decode, chunked prefill): whole sequences go to ranks, balanced by
   key count (longest first onto the least-loaded rank); no collective on the data path.
 * KV-sequence split (one long decode): rank r holds key positions [begin_r, end_r) of every
-  sequence; each rank computes a split-KV partial (o, m, l) per (sequence, q head) with
-  apex_attn_decode_partial_bf16, ONE all-gather exchanges the partials (16.5 KB per sequence
-  per rank at Hq=16, D=256) and every rank merges them with apex_attn_merge_partials.
+  sequence.  Fused form (PeerExchangeBuffers + apex_attn_decode_kvsplit_bf16): the decode
+  kernel writes each rank's partial (o, m, l) straight into every rank's gather buffer over
+  NVLink (CUDA IPC mappings), raises a per-step flag there and merges once all flags are in --
+  one launch per step.  Collective form (KVSplitDecode, the baseline): the partial from
+  apex_attn_decode_partial_bf16, ONE NCCL all-gather (16.5 KB per sequence per rank at Hq=16,
+  D=256) and apex_attn_merge_partials.
 
 The reference is single-device; these are new (docs/B6_3_attention.md has no parallelism).
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, List, Sequence, Tuple
 
 import torch
@@ -67,3 +71,93 @@ class KVSplitDecode:
         self.dist.all_gather_into_tensor(self.gathered.view(-1), self.partial.view(-1), group=self.group)
         merge_fn(self.gathered, out)
         return out
+
+
+class PeerExchangeBuffers:
+    """Exchange buffers of the fused KV-split decode (apex_attn_decode_kvsplit_bf16) for up to
+    `batch` sequences over the ranks of `group` (one process per GPU, all on one NVLink domain).
+
+    Each rank allocates its gather buffer, flag array and step counters with apex_device_alloc
+    (zeroed), shares the first two by CUDA IPC handle through one all_gather_object, and maps the
+    other ranks' buffers.  `exchange` is the apex_peer_exchange to pass to every decode step;
+    every rank must run the same number of steps.  close() unmaps and frees (collective)."""
+
+    def __init__(self, shape, batch: int, group=None):
+        import torch.distributed as dist
+        from . import _native
+        self._native, self.dist, self.group = _native, dist, group
+        lib = _native.load()
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world > _native.MAX_PEERS:
+            raise ValueError(f"PeerExchangeBuffers: at most {_native.MAX_PEERS} ranks")
+        self._own, self._opened = [], []
+        # Every rank takes the same collective steps whatever fails locally; a failure anywhere
+        # releases everything on every rank and raises on every rank.
+        handles, err = None, None
+        try:
+            sizes = [ctypes.c_size_t() for _ in range(3)]
+            _native.check(lib.apex_attn_peer_exchange_bytes(shape.c(), batch, self.world,
+                                                            *map(ctypes.byref, sizes)))
+            gather, flags, seq = (self._alloc(lib, n.value) for n in sizes)
+            handles = []
+            for ptr in (gather, flags):
+                h = (ctypes.c_uint8 * 64)()
+                _native.check(lib.apex_ipc_get_handle(ptr, h))
+                handles.append(bytes(h))
+        except Exception as e:  # noqa: BLE001 -- reported collectively below
+            handles, err = None, e
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, handles, group=group)
+        x = _native.PeerExchange()
+        if err is None and all(h is not None for h in everyone):
+            try:
+                x.rank, x.world, x.seq = self.rank, self.world, seq
+                for r in range(self.world):
+                    if r == self.rank:
+                        x.gather[r], x.flags[r] = gather, flags
+                        continue
+                    for i, h in enumerate(everyone[r]):
+                        ptr = ctypes.c_void_p()
+                        buf = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+                        _native.check(lib.apex_ipc_open_handle(buf, ctypes.byref(ptr)))
+                        self._opened.append(ptr.value)
+                        if i == 0:
+                            x.gather[r] = ptr.value
+                        else:
+                            x.flags[r] = ptr.value
+            except Exception as e:  # noqa: BLE001
+                err = e
+        ok = torch.tensor([0 if err is not None else 1], dtype=torch.int32, device="cuda")
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if int(ok.item()) == 0:
+            self.close()
+            raise RuntimeError(f"PeerExchangeBuffers: peer-memory exchange unavailable "
+                               f"({err!r} here)" if err else "PeerExchangeBuffers: failed on another rank")
+        self.exchange = x
+        torch.cuda.synchronize()
+
+    def _alloc(self, lib, nbytes: int) -> int:
+        ptr = ctypes.c_void_p()
+        self._native.check(lib.apex_device_alloc(max(int(nbytes), 16), ctypes.byref(ptr)))
+        self._own.append(ptr.value)
+        return ptr.value
+
+    def _release(self, lib) -> None:
+        for p in self._opened:
+            lib.apex_ipc_close_handle(p)
+        self._opened = []
+        for p in self._own:
+            lib.apex_device_free(p)
+        self._own = []
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, wait until every rank has done the same, free our own."""
+        lib = self._native.load()
+        torch.cuda.synchronize()
+        for p in self._opened:
+            lib.apex_ipc_close_handle(p)
+        self._opened = []
+        self.dist.barrier(group=self.group)
+        for p in self._own:
+            lib.apex_device_free(p)
+        self._own = []

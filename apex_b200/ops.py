@@ -19,6 +19,8 @@ from __future__ import annotations
 import math
 from dataclasses import dataclass
 
+import ctypes
+
 import torch
 
 from . import _native
@@ -192,6 +194,27 @@ def attention_decode_partial(shape: AttentionShape, q_raw, k_new, v_new, q_norm_
                                             partial.data_ptr(), workspace.buffer.data_ptr(),
                                             workspace.nbytes, _stream()))
     return partial
+
+
+def attention_decode_kvsplit(shape: AttentionShape, q_raw, k_new, v_new, q_norm_w, k_norm_w,
+                             cache: KvCache, seq_lens: torch.Tensor, max_seq_len: int,
+                             kv_begin: int, kv_end: int, exchange, out: torch.Tensor,
+                             workspace: DecodeWorkspace) -> torch.Tensor:
+    """KV-split decode step on keys [kv_begin, kv_end) held locally, merged with the other ranks
+    inside the kernel through NVLink peer memory (apex_attn_decode_kvsplit_bf16); `exchange` is
+    the _native.PeerExchange that apex_b200.dist.PeerExchangeBuffers built.  out [B,Hq,D] bf16
+    holds the full result on every rank."""
+    B = seq_lens.numel()
+    _check_decode(shape, q_raw, k_new, v_new, cache, seq_lens, B)
+    _need(out, torch.bfloat16, "out")
+    lib = _native.load()
+    check(lib.apex_attn_decode_kvsplit_bf16(shape.c(), q_raw.data_ptr(), k_new.data_ptr(),
+                                            v_new.data_ptr(), _ptr(q_norm_w), _ptr(k_norm_w),
+                                            cache.k.data_ptr(), cache.v.data_ptr(), cache.capacity,
+                                            seq_lens.data_ptr(), B, max_seq_len, kv_begin, kv_end,
+                                            ctypes.byref(exchange), out.data_ptr(),
+                                            workspace.buffer.data_ptr(), workspace.nbytes, _stream()))
+    return out
 
 
 def merge_partials(partials: torch.Tensor, out: torch.Tensor) -> torch.Tensor:

@@ -238,18 +238,29 @@ class DecodeWorkload:
             self.sets.append(s)
         self.lens_t = torch.tensor(self.lens, dtype=torch.int32, device=device)
         self.ws = ops.DecodeWorkspace(self.shape, B, L, device=device)
+        self.peer = None
         if self.kv_split:
+            # fused: partials merged inside the decode kernel through NVLink peer memory; if the
+            # peer mapping is unavailable on any rank, every rank uses the NCCL all-gather instead
             self.splitter = adist.KVSplitDecode(B, Hq, D, device)
+            try:
+                self.peer = adist.PeerExchangeBuffers(self.shape, B)
+            except RuntimeError as e:
+                self.peer_error = str(e)
             local = sum(2 * Hkv * max(0, min(Li, self.kv_end) - self.kv_begin) * D * 2 for Li in self.lens)
             self.bytes = local + 2 * B * Hq * D * 2
         else:
             self.bytes = decode_bytes(cfg, self.lens)
         self.tokens = B if not self.kv_split or rank == 0 else 0
-        self.launches_per_step = 2 if self.kv_split else 1
+        self.launches_per_step = 2 if self.kv_split and self.peer is None else 1
         self.kernel_name = "decode_splitkv_kernel"
 
     def _call(self, s):
-        if self.kv_split:
+        if self.peer is not None:
+            self.ops.attention_decode_kvsplit(self.shape, s["q"], s["k"], s["v"], self.qw, self.kw, s["cache"],
+                                              self.lens_t, self.L, self.kv_begin, self.kv_end, self.peer.exchange,
+                                              s["out"], self.ws)
+        elif self.kv_split:
             ops = self.ops
 
             def partial(p):
@@ -266,7 +277,7 @@ class DecodeWorkload:
 
     def dominant(self, i):
         s = self.sets[i % self.R]
-        if self.kv_split:
+        if self.kv_split and self.peer is None:
             p = self.splitter.partial
             self.ops.attention_decode_partial(self.shape, s["q"], s["k"], s["v"], self.qw, self.kw, s["cache"],
                                               self.lens_t, self.L, self.kv_begin, self.kv_end, p, self.ws)
@@ -653,11 +664,15 @@ def run_ours(args, cfg):
         for g in graphs.values():
             del g
         graphs.clear()
+        torch.cuda.synchronize()
+        if getattr(wl, "peer", None) is not None:
+            wl.peer.close()  # unmaps the peers' buffers on every rank before any rank frees its own
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    sharding = ("kv-split + all-gather" if getattr(wl, "kv_split", False)
+    sharding = (("kv-split + peer-memory merge" if getattr(wl, "peer", None) is not None
+                 else "kv-split + all-gather") if getattr(wl, "kv_split", False)
                 else "batch-shard" if (cfg.lens_range and world > 1)
                 else "head-shard" if getattr(wl, "head_shard", False) else "replica")
     line = {

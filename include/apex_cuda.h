@@ -171,6 +171,52 @@ APEX_API int apex_attn_decode_partial_bf16(const apex_attn_params *p, const uint
                                   float *partial, void *workspace, size_t workspace_bytes,
                                   void *stream);
 
+/* ------------------------------------------------------------------ KV split over GPUs, fused
+ * The reference runs on one device, so nothing here has a counterpart in it.  A KV range split
+ * over the GPUs of one NVLink domain is merged inside the decode kernel: each rank writes its
+ * partial (the apex_attn_decode_partial_bf16 record) straight into every rank's gather buffer
+ * over NVLink, raises a per-step flag there, waits for every rank's flag (bounded: on expiry the
+ * device status word reports a timeout) and merges.  One launch per step, no collective call.
+ *
+ * Buffers (per rank, zero-initialised, e.g. by apex_device_alloc; shared with the other ranks by
+ * apex_ipc_get_handle / apex_ipc_open_handle):
+ *   gather  [2][world][batch*q_heads][head_dim+4] f32   (two slots, alternating by step)
+ *   flags   [world][batch*kv_heads] uint32               (last step each rank published)
+ *   seq     [batch*kv_heads] uint32                      (this rank's step counters)
+ * Every rank must call apex_attn_decode_kvsplit_bf16 the same number of times with the same
+ * batch and the same world; calls on one rank are serialised (one stream). */
+typedef struct apex_peer_exchange {
+    uint32_t rank, world;       /* 1 <= world <= 8, rank < world */
+    float *gather[8];           /* gather[r]: rank r's gather buffer as mapped in this process, 16-byte aligned */
+    uint32_t *flags[8];         /* flags[r]: rank r's flag array as mapped in this process */
+    uint32_t *seq;              /* this rank's step counters */
+} apex_peer_exchange;
+
+/* Bytes of the three buffers above for `batch` sequences over `world` ranks. */
+APEX_API int apex_attn_peer_exchange_bytes(const apex_attn_params *p, uint32_t batch, uint32_t world,
+                                           size_t *gather_bytes, size_t *flag_bytes, size_t *seq_bytes);
+
+/* apex_attn_decode_partial_bf16 on this rank's key range [kv_begin, kv_end), then the exchange
+ * and merge above: out [B][Hq][D] bf16 holds the full decode output on every rank. */
+APEX_API int apex_attn_decode_kvsplit_bf16(const apex_attn_params *p, const uint16_t *q_raw,
+                                           const uint16_t *k_new, const uint16_t *v_new,
+                                           const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                                           uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
+                                           const int32_t *seq_lens, uint32_t batch, uint32_t max_seq_len,
+                                           uint32_t kv_begin, uint32_t kv_end, const apex_peer_exchange *x,
+                                           uint16_t *out, void *workspace, size_t workspace_bytes,
+                                           void *stream);
+
+/* Zeroed device memory from cudaMalloc (for buffers shared by CUDA IPC, which needs the base of
+ * an allocation), and its release.  No counterpart in the reference. */
+APEX_API int apex_device_alloc(size_t bytes, void **ptr);
+APEX_API int apex_device_free(void *ptr);
+/* CUDA IPC: a 64-byte handle for an apex_device_alloc pointer, the same memory opened in another
+ * process (peer access enabled on demand), and closing it.  No counterpart in the reference. */
+APEX_API int apex_ipc_get_handle(const void *ptr, void *handle64);
+APEX_API int apex_ipc_open_handle(const void *handle64, void **ptr);
+APEX_API int apex_ipc_close_handle(void *ptr);
+
 /* Log-sum-exp merge of num_partials partial sets laid out [num_partials][rows][D+2] (the
  * apex_attn_decode_partial_bf16 format, e.g. after an all-gather) into out [rows][D] bf16. */
 APEX_API int apex_attn_merge_partials(const float *partials, uint32_t num_partials, uint32_t rows,
