@@ -7,10 +7,12 @@
 // o = softmax(scale * q K^T) V over keys p - window < j <= p (or j <= p), GQA map h/(Hq/Hkv).
 //
 // Two launches per call:
-//  1. prep: one warp per (sequence, token, head group): the token's RoPE cos/sin are computed
-//     once and reused for its rows; every row is one 16-byte load and store per lane.  q goes to
-//     a head-major workspace [B][Hq][T][256] (one 3-D TMA box per 128-query tile), k and v to
-//     the caches.  It also zeroes the attention kernel's scheduler counters.
+//  1. prep: a persistent grid (two blocks per SM) streams each token's q, k and v rows into a
+//     4-stage shared-memory ring with 1-D TMA bulk copies (one producer warp, which also writes
+//     the token's RoPE cos/sin); eight consumer warps norm, rope and store the rows, one 16-byte
+//     load and store per lane per row.  q goes to a head-major workspace [B][Hq][T][256] (one
+//     3-D TMA box per 128-query tile), k and v to the caches.  It also zeroes the attention
+//     kernel's scheduler counters.
 //  2. attention: a persistent kernel of CTA pairs (clusters of two on two SMs).  A pair takes
 //     work items from an atomic counter, heaviest first: 256 query rows = the same 128 queries
 //     for the two q heads of a GQA group (head 2i+r in CTA r) when the group size is even,
@@ -674,109 +676,168 @@ struct PrepArgs {
     const uint16_t *q_raw, *k_raw, *v_raw, *q_w, *k_w;
     uint16_t *q_ws, *k_cache, *v_cache;
     unsigned *sched;
+    unsigned *status;     // device status word
     uint32_t B, T, pos0, q_heads, kv_heads, capacity, rope_pairs, qk_norm, v_norm;
     float eps;
     RopeTable rope;
 };
 
-// Prep work unit = (token, group): groups [0, nqg) are 8 q heads each, groups [nqg, nqg + nkg)
-// are 4 kv heads each (k and v).  A warp issues all loads of its unit (4 KB) before any math.
-// Lane l holds dims [4l, 4l+4) and [128+4l, 128+4l+4) of each row: both members of its four RoPE
-// pairs, so rotation needs no shuffles and each lane computes only its own four cos/sin.
-constexpr int kPrepThreads = 256;
+// A persistent grid of two blocks per SM walks the tokens (block i: tokens i, i + grid, ...).  Per
+// token, one producer warp copies the token's q rows, then k rows, then v rows (three contiguous
+// runs in the [B][T][heads][256] inputs, 16 KB at Hq = 16, Hkv = 8) into the next stage of a
+// 4-stage shared-memory ring with 1-D TMA bulk copies, and writes the token's RoPE cos/sin beside
+// it; eight consumer warps take rows w, w+8, ... of the stage: RMS norm (weights held in
+// registers), RoPE, bf16, one 16-byte load and store per lane per row.  Loads of later tokens
+// stay in flight while earlier ones are computed and stored.
+// Lane l holds dims [4l, 4l+4) and [128+4l, 128+4l+4) of a row: both members of its four RoPE pairs,
+// so rotation needs no shuffles.
+constexpr int kPrepConsumers = 8;
+constexpr int kPrepThreads = (kPrepConsumers + 1) * 32;
+constexpr int kPrepStages = 4;
+constexpr uint32_t kRowBytes = kD * 2;
+constexpr uint32_t kPrepMaxRows = 96;  // q + k + v rows of one token (shared memory: 4 x 48 KB)
+
+uint32_t prep_smem_bytes(uint32_t rows) { return kPrepStages * (rows * kRowBytes + kD * 4) + 2 * kPrepStages * 8; }
 
 __device__ __forceinline__ void unpack4(uint2 v, float (&x)[4]) {
     x[0] = bf16lo(v.x); x[1] = bf16hi(v.x); x[2] = bf16lo(v.y); x[3] = bf16hi(v.y);
 }
 __device__ __forceinline__ uint2 pack4(const float (&x)[4]) { return make_uint2(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3])); }
 
-// One warp per unit.  Lane l holds dims [4l, 4l+4) and [128+4l, 128+4l+4) of each of the unit's 8
-// rows (8 q rows, or 4 k rows then 4 v rows): all loads are issued first, then the 8 rows' RMS
-// reductions run interleaved, then each row is scaled, roped and stored.
-__global__ void __launch_bounds__(kPrepThreads) prefill_prep_kernel(const __grid_constant__ PrepArgs a) {
-    const uint32_t lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) griddep_launch_dependents();  // the attention kernel's set-up may start
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
+__global__ void __launch_bounds__(kPrepThreads, 2) prefill_prep_kernel(const __grid_constant__ PrepArgs a) {
+    extern __shared__ __align__(128) uint8_t psm[];
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) griddep_launch_dependents();  // the attention kernel's set-up may start
+    if (blockIdx.x == 0 && tid == 0) {
         a.sched[0] = 0;
         a.sched[1] = 0;
     }
-    const uint32_t nqg = (a.q_heads + 7) / 8, nkg = (a.kv_heads + 3) / 4, groups = nqg + nkg;
-    const uint32_t units = a.B * a.T * groups;  // below 2^31 (checked on the host)
-    const uint32_t warps = gridDim.x * (blockDim.x >> 5);
-    const uint32_t d_lo = 4 * lane, d_hi = kD / 2 + 4 * lane;
-    for (uint32_t u = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < units; u += warps) {
-        const uint32_t bt = u / groups, grp = u - bt * groups;
-        const uint32_t b = bt / a.T, t = bt - b * a.T;
-        const bool is_q = grp < nqg;
-        const uint32_t h0 = is_q ? grp * 8 : (grp - nqg) * 4;
-        const uint32_t n = is_q ? min(8u, a.q_heads - h0) : min(4u, a.kv_heads - h0);
-        // row i: q head h0+i, or k head h0+i (i < 4) / v head h0+i-4 (i >= 4)
-        uint2 raw[8][2];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t hi_ = is_q ? static_cast<uint32_t>(i) : static_cast<uint32_t>(i & 3);
-            if (hi_ < n) {
-                const uint16_t *src =
-                    is_q ? a.q_raw + (static_cast<uint64_t>(bt) * a.q_heads + h0 + hi_) * kD
-                         : (i < 4 ? a.k_raw : a.v_raw) + (static_cast<uint64_t>(bt) * a.kv_heads + h0 + hi_) * kD;
-                raw[i][0] = *reinterpret_cast<const uint2 *>(src + d_lo);
-                raw[i][1] = *reinterpret_cast<const uint2 *>(src + d_hi);
-            } else {
-                raw[i][0] = raw[i][1] = make_uint2(0u, 0u);
+    const uint32_t Hq = a.q_heads, Hkv = a.kv_heads, rows = Hq + 2 * Hkv;
+    const uint32_t stage_bytes = rows * kRowBytes;
+    float *tab = reinterpret_cast<float *>(psm + kPrepStages * stage_bytes);  // [stage][cos 128 | sin 128]
+    const uint32_t bars = smem_u32(psm + kPrepStages * (stage_bytes + kD * 4));
+    auto full = [&](uint32_t s) { return bars + 8u * s; };
+    auto empty = [&](uint32_t s) { return bars + 8u * (kPrepStages + s); };
+    if (tid == 0) {
+        for (int s = 0; s < kPrepStages; ++s) {
+            mbar_init(full(s), 32);  // the producer warp's lanes (after their cos/sin) + the copies' bytes
+            mbar_init(empty(s), kPrepConsumers);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const uint32_t ntok = a.B * a.T, G = gridDim.x;
+    if (warp == kPrepConsumers) {
+        // ---------------------------------------------------------------- producer warp
+        uint32_t n = 0;
+        for (uint32_t tok = blockIdx.x; tok < ntok; tok += G, ++n) {
+            const uint32_t s = n % kPrepStages;
+            if (n >= kPrepStages &&
+                !__all_sync(0xffffffffu, mbar_wait(empty(s), ((n / kPrepStages) - 1) & 1, a.status)))
+                break;
+            const uint32_t t = tok % a.T;
+            uint8_t *st = psm + s * stage_bytes;
+            if (lane == 0) {
+                mbar_expect_tx(full(s), stage_bytes);
+                tma_bulk_load(smem_u32(st), a.q_raw + static_cast<uint64_t>(tok) * Hq * kD, Hq * kRowBytes, full(s));
+                tma_bulk_load(smem_u32(st + Hq * kRowBytes), a.k_raw + static_cast<uint64_t>(tok) * Hkv * kD,
+                              Hkv * kRowBytes, full(s));
+                tma_bulk_load(smem_u32(st + (Hq + Hkv) * kRowBytes), a.v_raw + static_cast<uint64_t>(tok) * Hkv * kD,
+                              Hkv * kRowBytes, full(s));
             }
-        }
-        const float pos = static_cast<float>(a.pos0 + t);
-        float cs[4], sn[4], w[8];
-        const uint16_t *wsrc = is_q ? a.q_w : a.k_w;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            if (d_lo + e < a.rope_pairs) rope_sincos(pos * a.rope.inv_freq[d_lo + e], sn[e], cs[e]);
-            else cs[e] = 1.f, sn[e] = 0.f;
-            w[e] = wsrc ? __uint_as_float(static_cast<uint32_t>(wsrc[d_lo + e]) << 16) : 1.0f;
-            w[4 + e] = wsrc ? __uint_as_float(static_cast<uint32_t>(wsrc[d_hi + e]) << 16) : 1.0f;
-        }
-        float lo[8][4], hi[8][4], ss[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            unpack4(raw[i][0], lo[i]);
-            unpack4(raw[i][1], hi[i]);
-            ss[i] = 0.f;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) ss[i] += lo[i][e] * lo[i][e] + hi[i][e] * hi[i][e];
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) ss[i] += __shfl_xor_sync(0xffffffffu, ss[i], o);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const bool is_v = !is_q && i >= 4;
-            const bool norm = is_v ? a.v_norm != 0 : a.qk_norm != 0;
-            const float inv = norm ? rsqrtf(ss[i] * (1.0f / kD) + a.eps) : 1.0f;
+            const float pos = static_cast<float>(a.pos0 + t);
+            float *cs = tab + s * kD;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                lo[i][e] *= inv * (is_v ? 1.0f : w[e]);
-                hi[i][e] *= inv * (is_v ? 1.0f : w[4 + e]);
+                const uint32_t i = 4 * lane + e;
+                float c = 1.f, sn = 0.f;
+                if (i < a.rope_pairs) rope_sincos(pos * a.rope.inv_freq[i], sn, c);
+                cs[i] = c;
+                cs[kD / 2 + i] = sn;
             }
-            if (!is_v) {
+            mbar_arrive(full(s));
+        }
+        return;
+    }
+    // -------------------------------------------------------------------- consumer warps
+    const uint32_t d_lo = 4 * lane, d_hi = kD / 2 + 4 * lane;
+    float wq[8], wk[8];
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    if (d_lo + e < a.rope_pairs) {
+    for (int e = 0; e < 4; ++e) {
+        wq[e] = a.q_w ? bf16lo(static_cast<uint32_t>(a.q_w[d_lo + e])) : 1.f;
+        wq[4 + e] = a.q_w ? bf16lo(static_cast<uint32_t>(a.q_w[d_hi + e])) : 1.f;
+        wk[e] = a.k_w ? bf16lo(static_cast<uint32_t>(a.k_w[d_lo + e])) : 1.f;
+        wk[4 + e] = a.k_w ? bf16lo(static_cast<uint32_t>(a.k_w[d_hi + e])) : 1.f;
+    }
+    uint32_t n = 0;
+    for (uint32_t tok = blockIdx.x; tok < ntok; tok += G, ++n) {
+        const uint32_t s = n % kPrepStages;
+        if (!__all_sync(0xffffffffu, mbar_wait(full(s), (n / kPrepStages) & 1, a.status))) break;
+        const uint32_t b = tok / a.T, t = tok - b * a.T;
+        const uint8_t *st = psm + s * stage_bytes;
+        const float *cs_tab = tab + s * kD;
+        float cs[4], sn[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            cs[e] = cs_tab[d_lo + e];
+            sn[e] = cs_tab[kD / 2 + d_lo + e];
+        }
+        // rows warp, warp + 8, warp + 16, warp + 24 together (their RMS reductions interleave)
+        for (uint32_t base = warp; base < rows; base += 4 * kPrepConsumers) {
+            uint2 raw[4][2];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t r = base + i * kPrepConsumers;
+                if (r < rows) {
+                    raw[i][0] = *reinterpret_cast<const uint2 *>(st + r * kRowBytes + 8 * lane);
+                    raw[i][1] = *reinterpret_cast<const uint2 *>(st + r * kRowBytes + kRowBytes / 2 + 8 * lane);
+                } else {
+                    raw[i][0] = raw[i][1] = make_uint2(0u, 0u);
+                }
+            }
+            float lo[4][4], hi[4][4], ss[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                unpack4(raw[i][0], lo[i]);
+                unpack4(raw[i][1], hi[i]);
+                ss[i] = 0.f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) ss[i] += lo[i][e] * lo[i][e] + hi[i][e] * hi[i][e];
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) ss[i] += __shfl_xor_sync(0xffffffffu, ss[i], o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t r = base + i * kPrepConsumers;
+                if (r >= rows) continue;
+                const bool is_q = r < Hq, is_v = r >= Hq + Hkv;
+                const bool norm = is_v ? a.v_norm != 0 : a.qk_norm != 0;
+                const float inv = norm ? rsqrtf(ss[i] * (1.0f / kD) + a.eps) : 1.0f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    lo[i][e] *= inv * (is_v ? 1.0f : (is_q ? wq[e] : wk[e]));
+                    hi[i][e] *= inv * (is_v ? 1.0f : (is_q ? wq[4 + e] : wk[4 + e]));
+                }
+                if (!is_v) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
                         const float l = lo[i][e], h = hi[i][e];
                         lo[i][e] = l * cs[e] - h * sn[e];
                         hi[i][e] = h * cs[e] + l * sn[e];
                     }
-            }
-            const uint32_t hi_ = is_q ? static_cast<uint32_t>(i) : static_cast<uint32_t>(i & 3);
-            if (hi_ < n) {
+                }
                 uint16_t *dst =
-                    is_q ? a.q_ws + ((static_cast<uint64_t>(b) * a.q_heads + h0 + hi_) * a.T + t) * kD
-                         : (i < 4 ? a.k_cache : a.v_cache) +
-                               ((static_cast<uint64_t>(b) * a.kv_heads + h0 + hi_) * a.capacity + a.pos0 + t) * kD;
+                    is_q ? a.q_ws + ((static_cast<uint64_t>(b) * Hq + r) * a.T + t) * kD
+                         : (is_v ? a.v_cache : a.k_cache) +
+                               ((static_cast<uint64_t>(b) * Hkv + (r - Hq - (is_v ? Hkv : 0u))) * a.capacity + a.pos0 + t) * kD;
                 *reinterpret_cast<uint2 *>(dst + d_lo) = pack4(lo[i]);
                 *reinterpret_cast<uint2 *>(dst + d_hi) = pack4(hi[i]);
             }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty(s));  // this warp is done reading the stage
     }
 }
 
@@ -813,8 +874,10 @@ int validate_prefill(const apex_attn_params *p, uint32_t capacity, uint32_t batc
         return fail(APEX_ERR_INVALID_ARGUMENT, n + ": pos0 + tokens exceeds capacity");
     const uint64_t items = static_cast<uint64_t>(batch) * p->q_heads * ((tokens + kBM - 1) / kBM);
     if (items > 0x7fffffffull) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": problem too large for one launch");
-    const uint64_t prep_units = static_cast<uint64_t>(batch) * tokens * ((p->q_heads + 7) / 8 + (p->kv_heads + 3) / 4);
-    if (prep_units > 0x7fffffffull) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": problem too large for one launch");
+    if (static_cast<uint64_t>(batch) * tokens > 0xffffffffull)
+        return fail(APEX_ERR_INVALID_ARGUMENT, n + ": problem too large for one launch");
+    if (p->q_heads + 2 * p->kv_heads > kPrepMaxRows)
+        return fail(APEX_ERR_UNSUPPORTED, n + ": more than 96 q + k + v heads per token");
     const size_t need = ws_bytes(batch, tokens, p->q_heads);
     if (!workspace || workspace_bytes < need)
         return fail(APEX_ERR_WORKSPACE, n + ": workspace of " + std::to_string(need) + " bytes required");
@@ -834,10 +897,23 @@ int launch_prep(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t
     pa.capacity = capacity; pa.rope_pairs = p->rope_pairs; pa.qk_norm = p->qk_norm; pa.v_norm = p->v_norm;
     pa.eps = p->eps;
     rope_table(pa.rope.inv_freq, p->rope_pairs, kD, p->rope_base);
-    const uint64_t units = static_cast<uint64_t>(batch) * tokens * ((p->q_heads + 7) / 8 + (p->kv_heads + 3) / 4);
-    const uint32_t grid = static_cast<uint32_t>(
-        std::max<uint64_t>(1, std::min<uint64_t>((units + kPrepThreads / 32 - 1) / (kPrepThreads / 32), 32ull * sm_count())));
-    prefill_prep_kernel<<<grid, kPrepThreads, 0, s>>>(pa);
+    pa.status = device_status_ptr();
+    if (!pa.status) return fail(APEX_ERR_CUDA, "prefill prep: device status word unavailable");
+    const uint32_t rows = p->q_heads + 2 * p->kv_heads;
+    const uint32_t smem = prep_smem_bytes(rows);
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+        const int rc = check_cuda(cudaFuncSetAttribute(prefill_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       static_cast<int>(prep_smem_bytes(kPrepMaxRows))),
+                                  "prefill prep smem attribute");
+        if (rc) return rc;
+        attr_set[dev] = true;
+    }
+    const uint64_t ntok = static_cast<uint64_t>(batch) * tokens;
+    const uint32_t grid = static_cast<uint32_t>(std::max<uint64_t>(1, std::min<uint64_t>(ntok, 2ull * sm_count())));
+    prefill_prep_kernel<<<grid, kPrepThreads, smem, s>>>(pa);
     return check_cuda(cudaGetLastError(), "prefill prep launch");
 }
 
