@@ -583,6 +583,11 @@ def run_ours(args, cfg):
     torch.cuda.synchronize()
     sampler.sample()
     sampler.start()
+    if world > 1:
+        # Line the ranks' streams up on the device: a rank whose host reaches this point later
+        # would otherwise hold the others' first exchange, and that wait would count as their step.
+        align = torch.zeros(1, device=device)
+        dist.all_reduce(align)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     if use_graph:
