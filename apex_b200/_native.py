@@ -54,7 +54,7 @@ class PeerExchange(ctypes.Structure):
     """apex_peer_exchange (include/apex_cuda.h): every rank's exchange buffers as mapped here."""
     _fields_ = [("rank", ctypes.c_uint32), ("world", ctypes.c_uint32),
                 ("gather", ctypes.c_void_p * MAX_PEERS), ("flags", ctypes.c_void_p * MAX_PEERS),
-                ("seq", ctypes.c_void_p)]
+                ("seq", ctypes.c_void_p), ("wait_ns", ctypes.c_uint64)]
 
 
 _lib = None

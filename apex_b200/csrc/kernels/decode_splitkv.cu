@@ -66,8 +66,21 @@ struct DecodeArgs {
     float *peer_gather[kMaxPeers];    // rank r's [2 step parity][world][B*Hq][D+4] f32, mapped here
     unsigned *peer_flags[kMaxPeers];  // rank r's [world][B*Hkv] last published step
     unsigned *peer_seq;               // this rank's [B*Hkv] step counters
+    unsigned long long peer_wait_ns;  // bound of the wait for the other ranks' flags
     RopeTable rope;      // inv_freq[i] = rope_base^(-2i/256)
 };
+
+// Peer mode: a step counter or flag with this bit set is poisoned -- some rank's wait for this
+// (sequence, kv head) gave up, so the two-slot ordering of the gather buffers no longer holds.
+// Every later step of that pair on every rank reports a timeout and writes nothing.
+constexpr unsigned kPeerPoison = 0x80000000u;
+constexpr unsigned long long kPeerWaitDefaultNs = 1000000000ull;  // one second
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 struct __align__(16) DecodeSmem {
     uint8_t k[kStages][kStageBytes];
@@ -212,13 +225,21 @@ __device__ __forceinline__ void consumer_reduce(float (&v)[kG], float (&red)[kCo
 // partials into bf16 out.  Steps alternate between two gather slots, so a rank that runs ahead never
 // overwrites data a slower peer is still merging (it cannot start step k+2 before every peer has
 // published step k+1, which each peer does only after finishing step k).  The wait for the peers'
-// flags is bounded: on expiry the status word gets kStatusTimeout and the output is left unwritten.
+// flags is bounded (a.peer_wait_ns): on expiry, or when a peer's flag is poisoned, the status word
+// gets kStatusTimeout, the output is left unwritten, and this pair's counter and this rank's flag on
+// every peer are poisoned, so that no rank publishes into or merges from the gather slots again (the
+// ordering above assumed a wait that succeeded).
 __device__ void peer_publish_merge(const DecodeArgs &a, DecodeSmem &sm, uint32_t b, uint32_t kvh, uint32_t tid,
                                    uint32_t g, uint32_t d0, const float (&o)[4], float m, float l) {
     const uint32_t bhkv = gridDim.z * a.kv_heads, bkv = b * a.kv_heads + kvh;
     const uint64_t rows = static_cast<uint64_t>(gridDim.z) * a.q_heads;
     const uint64_t row = static_cast<uint64_t>(b) * a.q_heads + kvh * kG + g;
-    const unsigned seq = *reinterpret_cast<volatile unsigned *>(a.peer_seq + bkv) + 1u;
+    const unsigned prev = *reinterpret_cast<volatile unsigned *>(a.peer_seq + bkv);
+    if (prev & kPeerPoison) {  // an earlier step gave up: publish nothing, merge nothing
+        if (tid == 0) atomicOr(a.status, kStatusTimeout);
+        return;
+    }
+    const unsigned seq = prev + 1u;
     const uint32_t par = seq & 1u;
     for (uint32_t p = 0; p < a.world; ++p) {
         float *dst = a.peer_gather[p] + ((static_cast<uint64_t>(par) * a.world + a.rank) * rows + row) * kWsRec;
@@ -234,17 +255,28 @@ __device__ void peer_publish_merge(const DecodeArgs &a, DecodeSmem &sm, uint32_t
         __threadfence_system();  // every thread's stores above (ordered by the barrier) before the flags
         for (uint32_t p = 0; p < a.world; ++p) st_release_sys(a.peer_flags[p] + a.rank * bhkv + bkv, seq);
         const unsigned *mine = a.peer_flags[a.rank] + bkv;
-        const long long start = clock64();
+        const unsigned long long start = globaltimer_ns();
         bool ok = true;
         for (uint32_t r = 0; r < a.world && ok; ++r) {
-            while (static_cast<int>(ld_acquire_sys(mine + r * bhkv) - seq) < 0) {
-                if (clock64() - start > kWaitBudgetCycles) {
-                    atomicOr(a.status, kStatusTimeout);
+            for (;;) {
+                const unsigned f = ld_acquire_sys(mine + r * bhkv);
+                if (f & kPeerPoison) {  // that rank gave up on this pair
+                    ok = false;
+                    break;
+                }
+                if (static_cast<int>(f - seq) >= 0) break;
+                if (globaltimer_ns() - start > a.peer_wait_ns) {
                     ok = false;
                     break;
                 }
                 __nanosleep(64);
             }
+        }
+        if (!ok) {
+            atomicOr(a.status, kStatusTimeout);
+            a.peer_seq[bkv] = seq | kPeerPoison;
+            for (uint32_t p = 0; p < a.world; ++p)
+                st_release_sys(a.peer_flags[p] + a.rank * bhkv + bkv, seq | kPeerPoison);
         }
         sm.is_last = ok;
     }
@@ -649,16 +681,27 @@ int check_params(const apex_attn_params *p, const char *name) {
     return APEX_OK;
 }
 
-int launch_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t *k_new,
-                  const uint16_t *v_new, const uint16_t *q_w, const uint16_t *k_w,
-                  uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
-                  const int32_t *seq_lens, uint32_t batch, uint32_t max_seq_len,
-                  uint32_t kv_begin, uint32_t kv_end, bool partial_mode, uint16_t *out,
-                  float *partial_out, void *workspace, size_t workspace_bytes_given, void *stream,
-                  const char *name, const apex_peer_exchange *peer = nullptr) {
+// A validated decode launch: arguments and grid, or empty (batch 0: nothing to launch).
+struct DecodePlan {
+    DecodeArgs a{};
+    dim3 grid;
+    bool empty = false;
+};
+
+// Checks every argument of a decode call and fills `plan`; queues nothing.
+int plan_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t *k_new,
+                const uint16_t *v_new, const uint16_t *q_w, const uint16_t *k_w,
+                uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
+                const int32_t *seq_lens, uint32_t batch, uint32_t max_seq_len,
+                uint32_t kv_begin, uint32_t kv_end, bool partial_mode, uint16_t *out,
+                float *partial_out, void *workspace, size_t workspace_bytes_given,
+                const char *name, const apex_peer_exchange *peer, DecodePlan &plan) {
     int rc = check_params(p, name);
     if (rc) return rc;
-    if (batch == 0) return ok();
+    if (batch == 0) {
+        plan.empty = true;
+        return APEX_OK;
+    }
     if (batch > 65535) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": batch > 65535");
     if (!q_raw || !k_new || !v_new || !k_cache || !v_cache || !seq_lens ||
         (partial_mode && !peer ? !partial_out : !out))
@@ -690,7 +733,8 @@ int launch_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16
                                             " bytes required");
     if (!aligned16(workspace)) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": workspace must be 16-byte aligned");
 
-    DecodeArgs a{};
+    DecodeArgs &a = plan.a;
+    a = DecodeArgs{};
     a.q_raw = q_raw; a.k_new = k_new; a.v_new = v_new; a.q_w = q_w; a.k_w = k_w;
     a.k_cache = k_cache; a.v_cache = v_cache; a.seq_lens = seq_lens;
     a.out = out; a.partial_out = partial_out;
@@ -715,6 +759,7 @@ int launch_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16
             a.peer_flags[r] = peer->flags[r];
         }
         a.peer_seq = peer->seq;
+        a.peer_wait_ns = peer->wait_ns ? peer->wait_ns : kPeerWaitDefaultNs;
     }
     rope_table(a.rope.inv_freq, p->rope_pairs, kD, p->rope_base);
     a.status = device_status_ptr();
@@ -722,22 +767,41 @@ int launch_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16
     const uint32_t grid_x = std::max<uint32_t>(1, (std::max<uint32_t>(range_len, 1) + a.chunk - 1) / a.chunk);
     if (grid_x > max_splits)
         return fail(APEX_ERR_WORKSPACE, std::string(name) + ": internal split plan exceeds workspace");
+    plan.grid = dim3(grid_x, p->kv_heads, batch);
+    return APEX_OK;
+}
 
+// Queues the planned decode kernel on `stream`.
+int run_decode_plan(const DecodePlan &plan, void *stream, const char *name) {
+    if (plan.empty) return ok();
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr_set[dev]) {
-        rc = check_cuda(cudaFuncSetAttribute(decode_splitkv_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(sizeof(DecodeSmem))),
-                        "decode smem attribute");
+        const int rc = check_cuda(cudaFuncSetAttribute(decode_splitkv_kernel,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       static_cast<int>(sizeof(DecodeSmem))),
+                                  "decode smem attribute");
         if (rc) return rc;
         attr_set[dev] = true;
     }
-    const dim3 grid(grid_x, p->kv_heads, batch);
-    decode_splitkv_kernel<<<grid, kThreads, sizeof(DecodeSmem), static_cast<cudaStream_t>(stream)>>>(a);
-    rc = check_cuda(cudaGetLastError(), name);
+    decode_splitkv_kernel<<<plan.grid, kThreads, sizeof(DecodeSmem), static_cast<cudaStream_t>(stream)>>>(plan.a);
+    const int rc = check_cuda(cudaGetLastError(), name);
     return rc ? rc : ok();
+}
+
+int launch_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t *k_new,
+                  const uint16_t *v_new, const uint16_t *q_w, const uint16_t *k_w,
+                  uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
+                  const int32_t *seq_lens, uint32_t batch, uint32_t max_seq_len,
+                  uint32_t kv_begin, uint32_t kv_end, bool partial_mode, uint16_t *out,
+                  float *partial_out, void *workspace, size_t workspace_bytes_given, void *stream,
+                  const char *name, const apex_peer_exchange *peer = nullptr) {
+    DecodePlan plan;
+    const int rc = plan_decode(p, q_raw, k_new, v_new, q_w, k_w, k_cache, v_cache, capacity, seq_lens, batch,
+                               max_seq_len, kv_begin, kv_end, partial_mode, out, partial_out, workspace,
+                               workspace_bytes_given, name, peer, plan);
+    return rc ? rc : run_decode_plan(plan, stream, name);
 }
 
 }  // namespace
@@ -889,15 +953,17 @@ extern "C" int apex_attn_decode_bf16_noalloc(const apex_attn_params *p, const ui
     void *scratch = nullptr;
     rc = noalloc_scratch(&scratch);
     if (rc) return rc;
+    // Every argument is checked before anything is queued, so a rejected call leaves nothing on
+    // `stream` (no counter clear on the shared array either).
+    DecodePlan plan;
+    rc = plan_decode(p, q_raw, k_new, v_new, q_norm_w, k_norm_w, k_cache, v_cache, capacity, seq_lens, batch,
+                     max_seq_len, 0, 0xffffffffu, false, out, nullptr, scratch, kNoAllocScratchBytes, name,
+                     nullptr, plan);
+    if (rc) return rc;
     // The split counters must start at zero; the array keeps whatever the last call left.
-    const size_t counters_off = align256(static_cast<size_t>(batch) * p->q_heads *
-                                         max_splits_for(batch, p->kv_heads, msl) * kWsRec * sizeof(float));
-    rc = check_cuda(cudaMemsetAsync(static_cast<uint8_t *>(scratch) + counters_off, 0,
-                                    static_cast<size_t>(batch) * p->kv_heads * sizeof(unsigned),
+    rc = check_cuda(cudaMemsetAsync(plan.a.ws_count, 0, static_cast<size_t>(batch) * p->kv_heads * sizeof(unsigned),
                                     static_cast<cudaStream_t>(stream)),
                     "apex_attn_decode_bf16_noalloc: clear counters");
     if (rc) return rc;
-    return launch_decode(p, q_raw, k_new, v_new, q_norm_w, k_norm_w, k_cache, v_cache, capacity, seq_lens,
-                         batch, max_seq_len, 0, 0xffffffffu, false, out, nullptr, scratch,
-                         kNoAllocScratchBytes, stream, name);
+    return run_decode_plan(plan, stream, name);
 }

@@ -145,7 +145,8 @@ APEX_API int apex_attn_decode_bf16(const apex_attn_params *p, const uint16_t *q_
  *   - The first call on each device looks up the array's device address (once per device);
  *     make that first call before any stream capture.
  *   - Allocates nothing: no cudaMalloc, no cudaFree, no allocating library routine.  Each
- *     call clears the scratch counters it needs on `stream` before the kernel.
+ *     call clears the scratch counters it needs on `stream` before the kernel.  Every argument
+ *     is checked first: a rejected call queues nothing on `stream`.
  *   - Every call shares the one array: calls whose execution overlaps on the GPU (other
  *     streams, other host threads) race and corrupt each other's results; serialise them. */
 APEX_API int apex_attn_decode_bf16_noalloc(const apex_attn_params *p, const uint16_t *q_raw,
@@ -184,12 +185,21 @@ APEX_API int apex_attn_decode_partial_bf16(const apex_attn_params *p, const uint
  *   flags   [world][batch*kv_heads] uint32               (last step each rank published)
  *   seq     [batch*kv_heads] uint32                      (this rank's step counters)
  * Every rank must call apex_attn_decode_kvsplit_bf16 the same number of times with the same
- * batch and the same world; calls on one rank are serialised (one stream). */
+ * batch and the same world; calls on one rank are serialised (one stream).
+ *
+ * Failure: the wait for the other ranks' flags gives up after wait_ns (0 = one second).  The
+ * step then leaves `out` unwritten for that (sequence, kv head), the device status word reports
+ * a timeout (apex_cuda_device_status returns APEX_ERR_DEVICE_TIMEOUT), and the pair's step counter
+ * and this rank's flag on every peer are poisoned: every later step of that pair, on every rank,
+ * reports a timeout and publishes and merges nothing (a rank that went on after a failed wait
+ * could otherwise overwrite a gather slot a slow peer still reads).  After APEX_ERR_DEVICE_TIMEOUT
+ * all ranks must stop and build new, zeroed exchange buffers before the next KV-split step. */
 typedef struct apex_peer_exchange {
     uint32_t rank, world;       /* 1 <= world <= 8, rank < world */
     float *gather[8];           /* gather[r]: rank r's gather buffer as mapped in this process, 16-byte aligned */
     uint32_t *flags[8];         /* flags[r]: rank r's flag array as mapped in this process */
     uint32_t *seq;              /* this rank's step counters */
+    uint64_t wait_ns;           /* bound of the wait for the other ranks, in ns; 0 = 1 s */
 } apex_peer_exchange;
 
 /* Bytes of the three buffers above for `batch` sequences over `world` ranks. */

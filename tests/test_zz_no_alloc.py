@@ -46,12 +46,15 @@ def _no_alloc(shape, c):
     cache_k, cache_v = c["kc"].clone(), c["vc"].clone()
     out = torch.empty_like(c["q"])
     p = shape.c()
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]      # cudaMemGetInfo around the call alone
     rc = lib.apex_attn_decode_bf16_noalloc(
         ctypes.byref(p), c["q"].data_ptr(), c["k"].data_ptr(), c["v"].data_ptr(), c["qw"].data_ptr(),
         c["kw"].data_ptr(), cache_k.data_ptr(), cache_v.data_ptr(), c["cap"], c["lens"].data_ptr(),
         c["lens"].numel(), c["max_len"], out.data_ptr(), torch.cuda.current_stream().cuda_stream)
     _native.check(rc)
-    return out, cache_k
+    torch.cuda.synchronize()
+    return out, cache_k, free_before - torch.cuda.mem_get_info()[0]
 
 
 def _close(a, b):
@@ -64,11 +67,14 @@ def test_no_alloc_decode_matches_workspace_decode_on_two_calls_in_a_row():
     shape = ops.AttentionShape(16, 8, 256, 128, 1e6, 0, 1 / 16, 1e-6, True, False)
     first = _case(61, [5000, 513, 8192, 77, 3001], 8192)
     second = _case(62, [1024, 1], 1024)                 # different shape: stale scratch must not leak
-    for c in (first, second):
+    for i, c in enumerate((first, second)):
         want = _with_workspace(shape, c)
-        got, cache_k = _no_alloc(shape, c)
-        torch.cuda.synchronize()
+        got, cache_k, allocated = _no_alloc(shape, c)
         _close(got, want)
+        if i == 1:
+            # the first call may load the library's device code (and with it the static array);
+            # the second must not change the device's free memory at all
+            assert allocated == 0, f"device free memory changed by {allocated} bytes"
         # the new token's key was appended at position seq_lens[b]-1, as the workspace path does
         L = int(c["lens"][0].item())
         assert not torch.equal(cache_k[0, :, L - 1], c["kc"][0, :, L - 1])
@@ -85,3 +91,25 @@ def test_no_alloc_decode_rejects_requests_beyond_its_scratch():
                                            fake, 1024, 131072, fake, None)
     assert rc == _native.APEX_ERR_WORKSPACE
     assert b"static scratch" in lib.apex_cuda_last_error()
+
+
+def test_no_alloc_decode_rejected_call_queues_nothing():
+    """A call rejected for a bad argument (here a misaligned cache pointer) returns before it
+    queues anything, so a stream capture around it records no node."""
+    shape = ops.AttentionShape(16, 8, 256, 128, 1e6, 0, 1 / 16, 1e-6, True, False)
+    c = _case(63, [100], 128)
+    _no_alloc(shape, c)  # the first call on a device comes before any capture
+    lib = _native.load()
+    p = shape.c()
+    out = torch.empty_like(c["q"])
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        rc = lib.apex_attn_decode_bf16_noalloc(
+            ctypes.byref(p), c["q"].data_ptr(), c["k"].data_ptr(), c["v"].data_ptr(), c["qw"].data_ptr(),
+            c["kw"].data_ptr(), c["kc"].data_ptr() + 2, c["vc"].data_ptr(), c["cap"], c["lens"].data_ptr(), 1,
+            c["max_len"], out.data_ptr(), stream.cuda_stream)
+    assert rc == _native.APEX_ERR_INVALID_ARGUMENT
+    assert b"aligned" in lib.apex_cuda_last_error()
+    del g
