@@ -16,8 +16,10 @@ APEX_ERR_UNSUPPORTED = 2
 APEX_ERR_CUDA = 3
 APEX_ERR_WORKSPACE = 4
 APEX_ERR_DEVICE_TIMEOUT = 5
+APEX_ERR_FORMAT = 6
 
-_ERR_NAMES = {1: "invalid argument", 2: "unsupported", 3: "CUDA error", 4: "workspace", 5: "device timeout"}
+_ERR_NAMES = {1: "invalid argument", 2: "unsupported", 3: "CUDA error", 4: "workspace", 5: "device timeout",
+              6: "format"}
 
 # Every entry point declared in include/apex_cuda.h.
 EXPORTED = (
@@ -29,6 +31,9 @@ EXPORTED = (
     "apex_attn_prefill_prep_bf16", "apex_attn_prefill_attend_bf16", "apex_attn_decode_bf16_noalloc",
     "apex_attn_peer_exchange_bytes", "apex_attn_decode_kvsplit_bf16", "apex_device_alloc",
     "apex_device_free", "apex_ipc_get_handle", "apex_ipc_open_handle", "apex_ipc_close_handle",
+    # include/apex_loader.h
+    "apex_model_open", "apex_model_close", "apex_model_summary_get", "apex_model_tensor", "apex_model_expert_piece",
+    "apex_model_verify", "apex_model_upload_core", "apex_model_load_expert",
 )
 
 
@@ -55,6 +60,17 @@ class PeerExchange(ctypes.Structure):
     _fields_ = [("rank", ctypes.c_uint32), ("world", ctypes.c_uint32),
                 ("gather", ctypes.c_void_p * MAX_PEERS), ("flags", ctypes.c_void_p * MAX_PEERS),
                 ("seq", ctypes.c_void_p), ("wait_ns", ctypes.c_uint64)]
+
+
+class ModelSummary(ctypes.Structure):
+    """apex_model_summary (include/apex_loader.h)."""
+    _fields_ = [("core_size", ctypes.c_uint64), ("alignment", ctypes.c_uint64), ("expert_slot_size", ctypes.c_uint64)] + \
+        [(n, ctypes.c_uint32) for n in ("core_tensors", "layer_files", "num_hidden_layers", "hidden_size",
+                                        "num_attention_heads", "num_key_value_heads", "head_dim", "global_head_dim",
+                                        "num_global_key_value_heads", "sliding_window", "num_experts",
+                                        "quant_group_size", "quant_bits")] + \
+        [(n, ctypes.c_float) for n in ("rms_norm_eps", "rope_theta_sliding", "rope_theta_full",
+                                       "partial_rotary_factor_full")]
 
 
 _lib = None
@@ -101,9 +117,19 @@ def load(path: str | pathlib.Path | None = None):
     L.apex_attn_prefill_bf16.argtypes = ([_PP] + [_vp] * 7 + [_u32, _u32, _u32, _u32, _vp, _vp, _sz, _vp])
     L.apex_attn_prefill_prep_bf16.argtypes = ([_PP] + [_vp] * 7 + [_u32, _u32, _u32, _u32, _vp, _sz, _vp])
     L.apex_attn_prefill_attend_bf16.argtypes = ([_PP, _vp, _sz, _vp, _vp] + [_u32, _u32, _u32, _u32, _vp, _vp])
+    _PU64 = ctypes.POINTER(ctypes.c_uint64)
+    L.apex_model_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(_vp)]
+    L.apex_model_close.argtypes = [_vp]
+    L.apex_model_close.restype = None
+    L.apex_model_summary_get.argtypes = [_vp, ctypes.POINTER(ModelSummary)]
+    L.apex_model_tensor.argtypes = [_vp, ctypes.c_char_p, _PU64, _PU64]
+    L.apex_model_expert_piece.argtypes = [_vp, ctypes.c_char_p, _PU64, _PU64]
+    L.apex_model_verify.argtypes = [_vp]
+    L.apex_model_upload_core.argtypes = [_vp, _vp, _sz, _i32, _vp, ctypes.POINTER(ctypes.c_double)]
+    L.apex_model_load_expert.argtypes = [_vp, _u32, _u32, _vp, _sz, _i32, _vp]
     for fn in EXPORTED:
         if fn not in ("apex_cuda_last_error", "apex_attn_decode_workspace_bytes",
-                      "apex_attn_prefill_workspace_bytes"):
+                      "apex_attn_prefill_workspace_bytes", "apex_model_close"):
             getattr(L, fn).restype = _i32
     _lib = L
     return L

@@ -31,7 +31,7 @@ NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompil
               "--expt-relaxed-constexpr", "-I", str(ROOT / "include")]
 
 KERNEL_SOURCES = sorted((CSRC / "kernels").glob("*.cu"))
-BACKEND_SOURCES = sorted((CSRC / "backend" / "cuda").glob("*.cpp"))
+BACKEND_SOURCES = sorted((CSRC / "backend" / "cuda").glob("*.cpp")) + sorted((CSRC / "loader").glob("*.cpp"))
 CLI_SOURCES = [CSRC / "main.cpp"]
 
 

@@ -4,6 +4,8 @@
 //   apex_cuda_cli device
 //   apex_cuda_cli bench-attn prefill <tokens> <window> [steps]
 //   apex_cuda_cli bench-attn decode <context> <batch> [steps]
+//   apex_cuda_cli manifest <packed_dir>       (the reference's `apex manifest`, src/main.cpp:36-49)
+//   apex_cuda_cli load <packed_dir>           (core.bin into HBM with digest checks, timed)
 //
 // bench-attn runs the bf16 operators of ops.h on synthetic inputs through the Backend
 // interface (allocate / run / sync) and prints the phase table and the memory ledger.
@@ -14,10 +16,12 @@
 #include <cstdlib>
 #include <cstring>
 #include <random>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
 #include "backend/cuda/cuda_backend.h"
+#include "loader/model_info.h"
 #include "ops.h"
 
 namespace {
@@ -123,11 +127,48 @@ int run_bench(const std::string &kind, uint32_t a, uint32_t b, int steps) {
     return 0;
 }
 
+// Prints the packed model's metadata without reading weight files.
+int run_manifest(const std::string &dir) {
+    const apex::ModelInfo m = apex::ModelInfo::load(dir);
+    std::printf("core tensors: %zu\n", m.core.size());
+    std::printf("core bytes: %llu\n", static_cast<unsigned long long>(m.core_size));
+    std::printf("expert stride: %llu\n", static_cast<unsigned long long>(m.expert_slot_size));
+    std::printf("layer files: %zu\n", m.layers.size());
+    if (m.core.count("norm.weight"))
+        std::printf("norm.weight offset: %llu\n", static_cast<unsigned long long>(m.getTensor("norm.weight").offset));
+    return 0;
+}
+
+// Copies core.bin into one device allocation (checking every tensor's digest on the way) and one
+// expert slot of layer 0, and prints the rates.
+int run_load(const std::string &dir) {
+    const apex::ModelInfo m = apex::ModelInfo::load(dir);
+    void *core = nullptr;
+    if (cudaMalloc(&core, m.core_size) != cudaSuccess) throw std::runtime_error("cudaMalloc of core.bin failed");
+    const apex::LoadStats s = apex::uploadCore(m, core, m.core_size, true, nullptr);
+    std::printf("core.bin: %.3f GB in %.3f s (%.2f GB/s)%s%s\n", s.bytes / 1e9, s.seconds, s.bytes / 1e9 / s.seconds,
+                s.mismatch.empty() ? "" : ", digest mismatch: ", s.mismatch.c_str());
+    int failures = s.mismatch.empty() ? 0 : 1;
+    if (!m.layers.empty()) {
+        void *slot = nullptr;
+        if (cudaMalloc(&slot, m.expert_slot_size) != cudaSuccess) throw std::runtime_error("cudaMalloc of a slot failed");
+        const apex::LoadStats e = apex::loadExpert(m, m.layers.front().layer, 0, slot, m.expert_slot_size, true, nullptr);
+        std::printf("expert slot: %llu bytes in %.3f ms%s%s\n", static_cast<unsigned long long>(e.bytes), e.seconds * 1e3,
+                    e.mismatch.empty() ? "" : ", digest mismatch: ", e.mismatch.c_str());
+        failures += e.mismatch.empty() ? 0 : 1;
+        cudaFree(slot);
+    }
+    cudaFree(core);
+    return failures;
+}
+
 }  // namespace
 
 int main(int argc, char **argv) {
     try {
         if (argc == 2 && std::strcmp(argv[1], "device") == 0) return run_device();
+        if (argc == 3 && std::strcmp(argv[1], "manifest") == 0) return run_manifest(argv[2]);
+        if (argc == 3 && std::strcmp(argv[1], "load") == 0) return run_load(argv[2]);
         if (argc >= 5 && std::strcmp(argv[1], "bench-attn") == 0) {
             const int steps = argc >= 6 ? std::atoi(argv[5]) : 20;
             return run_bench(argv[2], static_cast<uint32_t>(std::atoi(argv[3])),
@@ -139,6 +180,7 @@ int main(int argc, char **argv) {
     }
     std::fprintf(stderr,
                  "usage: apex_cuda_cli device | apex_cuda_cli bench-attn prefill <tokens> <window> [steps] | "
-                 "apex_cuda_cli bench-attn decode <context> <batch> [steps]\n");
+                 "apex_cuda_cli bench-attn decode <context> <batch> [steps] | apex_cuda_cli manifest <packed_dir> | "
+                 "apex_cuda_cli load <packed_dir>\n");
     return 2;
 }

@@ -1,5 +1,5 @@
-"""CPU tests of the C ABI library: it loads, exports every entry point include/apex_cuda.h
-declares, and rejects bad arguments before touching a GPU."""
+"""CPU tests of the C ABI library: it loads, exports every entry point include/*.h declares, and
+rejects bad arguments before touching a GPU."""
 from __future__ import annotations
 
 import ctypes
@@ -13,11 +13,14 @@ from apex_b200 import _native
 from apex_b200._native import AttnParams
 
 ROOT = pathlib.Path(__file__).resolve().parents[1]
-HEADER = ROOT / "include" / "apex_cuda.h"
+HEADERS = sorted((ROOT / "include").glob("*.h"))
 
 
 def declared():
-    return sorted(set(re.findall(r"APEX_API\s+[\w\s\*]*?\b(apex_\w+)\s*\(", HEADER.read_text())))
+    names = set()
+    for h in HEADERS:
+        names |= set(re.findall(r"APEX_API\s+[\w\s\*]*?\b(apex_\w+)\s*\(", h.read_text()))
+    return sorted(names)
 
 
 def test_header_declares_what_the_binding_knows():
