@@ -33,13 +33,21 @@ namespace {
 
 constexpr int kD = 256;                 // head_dim
 constexpr int kG = 2;                   // q heads per kv head (GQA group)
+constexpr int kPosPerWarp = 8;          // positions one consumer warp takes from a stage
+constexpr int kRowBytes = kD * 2;
+// Split-KV form: 4 consumer warps, stages of 32 positions, a 3-stage ring, 2 CTAs per SM.
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStagePos = 32;
+constexpr int kStagePos = kConsumerWarps * kPosPerWarp;
 constexpr int kStages = 3;
-constexpr int kRowBytes = kD * 2;
 constexpr int kStageBytes = kStagePos * kRowBytes;
-constexpr int kPosPerWarp = kStagePos / kConsumerWarps;
+// Cluster form (short contexts): 8 consumer warps, stages of 64 positions, a 1- or 2-stage ring; the
+// splits of one (sequence, kv head) form one thread-block cluster and merge in the leader CTA's
+// shared memory.
+constexpr int kShortWarps = 8;
+constexpr int kShortStagePos = kShortWarps * kPosPerWarp;
+constexpr uint32_t kMaxCluster = 16;
+constexpr uint32_t kShortMaxLen = 4096;  // longest context the cluster form is chosen for
 constexpr int kPart = kD + 2;           // public partial record: o[D], m, l
 constexpr int kWsRec = kD + 4;          // workspace record: o[D], m, l, pad (16-byte multiple)
 constexpr float kLog2e = 1.4426950408889634f;
@@ -82,18 +90,22 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
     return t;
 }
 
-struct __align__(16) DecodeSmem {
-    uint8_t k[kStages][kStageBytes];
-    uint8_t v[kStages][kStageBytes];
+template <int CW, int ST, bool CL>
+struct __align__(16) DecodeSmemT {
+    uint8_t k[ST][CW * kPosPerWarp * kRowBytes];
+    uint8_t v[ST][CW * kPosPerWarp * kRowBytes];
     float q[kG][kD];
     uint16_t new_k[kD];
     uint16_t new_v[kD];
     float rope_cs[kD / 2], rope_sn[kD / 2];  // cos, sin of the new position per pair
-    float wm[kConsumerWarps][kG], wl[kConsumerWarps][kG];
-    float red[kConsumerWarps][kG];
-    uint64_t full[kStages], empty[kStages];
+    float wm[CW][kG], wl[CW][kG];
+    float red[CW][kG];
+    float parts[CL ? kMaxCluster : 1][kG][kWsRec];  // cluster form: every split's partial (leader)
+    uint64_t full[ST], empty[ST];
+    uint64_t gather;                                 // cluster form: one arrival per split (leader)
     int is_last;
 };
+using DecodeSmem = DecodeSmemT<kConsumerWarps, kStages, false>;
 
 __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -103,9 +115,20 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+template <int CW = kConsumerWarps>
 __device__ __forceinline__ void consumer_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
 }
+// Cluster barrier halves (not warp-aligned: the producer warp's lanes diverge).
+__device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+// Store two floats into another CTA's shared memory (cluster address), counted in bytes on that
+// CTA's mbarrier (complete_tx): the receiver's wait on the barrier is all the ordering needed.
+__device__ __forceinline__ void st_async_f32x2(uint32_t addr, float x, float y, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+                 "f"(x), "f"(y), "r"(remote_bar)
+                 : "memory");
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
 
 // Online-softmax update of one warp with up to 8 key/value rows (row j at kbase/vbase +
 // j*512 bytes in shared memory).  State: m[g] (log2 units, warp-uniform), lpart (this lane's
@@ -181,24 +204,34 @@ __device__ __forceinline__ void warp_step(const uint8_t *kbase, const uint8_t *v
         for (int e = 0; e < 8; ++e) acc[g][e] *= alpha[g];
         m[g] = m_new[g];
     }
-    for (int j = 0; j < nvalid; ++j) {
-        const float p0 = __shfl_sync(0xffffffffu, p, 4 * j);
-        const float p1 = __shfl_sync(0xffffffffu, p, 4 * j + 2);
-        const uint4 raw = *reinterpret_cast<const uint4 *>(vbase + j * kRowBytes + lane * 16);
+    // Every probability and V row first (independent shuffles and shared loads in flight together),
+    // then the accumulation.  Rows past nvalid read as zero (their p is 0; stale shared memory
+    // could hold non-finite bits).
+    float p0[kPosPerWarp], p1[kPosPerWarp];
+    uint4 vraw[kPosPerWarp];
+#pragma unroll
+    for (int j = 0; j < kPosPerWarp; ++j) {
+        p0[j] = __shfl_sync(0xffffffffu, p, 4 * j);
+        p1[j] = __shfl_sync(0xffffffffu, p, 4 * j + 2);
+        vraw[j] = j < nvalid ? *reinterpret_cast<const uint4 *>(vbase + j * kRowBytes + lane * 16)
+                             : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int j = 0; j < kPosPerWarp; ++j) {
         float vf[8];
-        unpack8(raw, vf);
+        unpack8(vraw[j], vf);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            acc[0][e] = fmaf(p0, vf[e], acc[0][e]);
-            acc[1][e] = fmaf(p1, vf[e], acc[1][e]);
+            acc[0][e] = fmaf(p0[j], vf[e], acc[0][e]);
+            acc[1][e] = fmaf(p1[j], vf[e], acc[1][e]);
         }
     }
 }
 
 // Max (or sum) over the 128 consumer threads of one value per head, using red[][] in shared
 // memory; every consumer thread gets the result.
-template <bool kMax>
-__device__ __forceinline__ void consumer_reduce(float (&v)[kG], float (&red)[kConsumerWarps][kG], uint32_t warp,
+template <bool kMax, int CW = kConsumerWarps>
+__device__ __forceinline__ void consumer_reduce(float (&v)[kG], float (&red)[CW][kG], uint32_t warp,
                                                 uint32_t lane) {
 #pragma unroll
     for (int g = 0; g < kG; ++g) {
@@ -214,10 +247,10 @@ __device__ __forceinline__ void consumer_reduce(float (&v)[kG], float (&red)[kCo
     for (int g = 0; g < kG; ++g) {
         float r = red[0][g];
 #pragma unroll
-        for (int w = 1; w < kConsumerWarps; ++w) r = kMax ? fmaxf(r, red[w][g]) : r + red[w][g];
+        for (int w = 1; w < CW; ++w) r = kMax ? fmaxf(r, red[w][g]) : r + red[w][g];
         v[g] = r;
     }
-    consumer_sync();
+    consumer_sync<CW>();
 }
 
 // Peer mode: publish this rank's partial of (b, kv head) -- thread t holds head g = t / 64, dims
@@ -309,13 +342,60 @@ __device__ void peer_publish_merge(const DecodeArgs &a, DecodeSmem &sm, uint32_t
     *reinterpret_cast<uint2 *>(a.out + row * kD + d0) = packed;
 }
 
-__global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __grid_constant__ DecodeArgs a) {
+// The decode step, in two forms.
+//   CL = false (CW = 4, ST = 3): split-KV.  Any number of splits per (b, kv head); the last CTA of
+//     each (found with an atomic counter, no spinning) merges the split partials from the
+//     workspace.  Also the partial and peer (KV split over GPUs) modes.
+//   CL = true (CW = 8, ST = 1 or 2): the splits of one (b, kv head) are one thread-block cluster
+//     of gridDim.x <= 16 CTAs.  Every split pushes its partial into the leader CTA's shared memory
+//     with asynchronous distributed-shared-memory stores counted on the leader's mbarrier, and the
+//     leader merges -- no workspace round trip, no fence + atomic, no second pass through L2, which
+//     at short contexts is most of the step.  No CTA returns before its pushes are issued.
+// Global attention (window 0): a split's first stage does not depend on the sequence length, so the
+// producer requests it before anything else -- before the length load -- and the consumers mask the
+// rows past the length (the cache holds `capacity` positions, so the extra rows are in bounds).
+template <int CW, int ST, bool CL>
+__global__ void __launch_bounds__((CW + 1) * 32, (CL && ST > 1) ? 1 : 2)
+    decode_kernel(const __grid_constant__ DecodeArgs a) {
+    using Smem = DecodeSmemT<CW, ST, CL>;
+    constexpr int SP = CW * kPosPerWarp;          // positions per stage
+    constexpr int DPT = kG * kD / (CW * 32);      // output dims per consumer thread in the merges
+    static_assert(CL || CW == kConsumerWarps, "the split-KV form has 4 consumer warps");
+    static_assert(!CL || DPT == 2, "the cluster form pushes two dims per thread");
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    DecodeSmem &sm = *reinterpret_cast<DecodeSmem *>(smem_raw);
+    Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const uint32_t Hq = a.q_heads;
+    const uint64_t head_base =
+        (static_cast<uint64_t>(b) * a.kv_heads + kvh) * a.capacity * kD;  // element offset
+
+    // ---- barriers and the speculative first stage, by the producer lane, before the length load
+    const uint32_t spec_off = split * a.chunk;  // local cache index of this split's first key (window 0)
+    const uint32_t spec_rows = (a.window == 0 && spec_off < a.capacity) ? min(static_cast<uint32_t>(SP), a.capacity - spec_off) : 0u;
+    if (warp == CW && lane == 0) {
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(smem_u32(&sm.full[s]), 1);
+            mbar_init(smem_u32(&sm.empty[s]), CW);
+        }
+        if constexpr (CL) mbar_init(smem_u32(&sm.gather), 1);
+        fence_mbar_init();
+        if (spec_rows) {
+            const uint32_t full = smem_u32(&sm.full[0]);
+            mbar_arrive_expect_tx(full, 2 * spec_rows * kRowBytes);
+            tma_bulk_load(smem_u32(sm.k[0]), a.k_cache + head_base + static_cast<uint64_t>(spec_off) * kD,
+                          spec_rows * kRowBytes, full);
+            tma_bulk_load(smem_u32(sm.v[0]), a.v_cache + head_base + static_cast<uint64_t>(spec_off) * kD,
+                          spec_rows * kRowBytes, full);
+        }
+        // cluster form, leader: every split's partial (two heads x (D + 2) floats) is expected here
+        if constexpr (CL)
+            if (split == 0) mbar_arrive_expect_tx(smem_u32(&sm.gather), gridDim.x * kG * (kD + 2) * 4);
+    }
+    __syncthreads();
+    // cluster form: every CTA's barriers are initialised before any CTA reaches the pushes below
+    if constexpr (CL) cluster_arrive_relaxed();
 
     // ---- key range of this (b, kv head) and of this split (global positions)
     const int32_t L = a.seq_lens[b];
@@ -330,47 +410,49 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
     const uint32_t n_keys = ke > kb ? ke - kb : 0;
     const uint32_t nsplit = n_keys ? (n_keys + a.chunk - 1) / a.chunk : 1;
     if (bad && split == 0 && tid == 0 && kvh == 0) atomicOr(a.status, kStatusBadLength);
-    if (split >= nsplit) return;
-    if (nsplit > a.max_splits) {  // cannot happen for lengths <= max_seq_len
-        if (tid == 0) atomicOr(a.status, kStatusBadLength);
-        return;
+    // A cluster split without keys still takes part: it pushes an empty partial (l = 0).
+    bool idle = split >= nsplit;
+    if constexpr (!CL) {
+        if (idle || nsplit > a.max_splits) {  // the second cannot happen for lengths <= max_seq_len
+            if (!idle && tid == 0) atomicOr(a.status, kStatusBadLength);
+            // the speculative copy lands before the CTA leaves
+            if (spec_rows && tid == 0) mbar_wait(smem_u32(&sm.full[0]), 0, a.status);
+            return;
+        }
+    } else if (nsplit > gridDim.x) {  // cannot happen for lengths <= max_seq_len
+        if (split == 0 && tid == 0) atomicOr(a.status, kStatusBadLength);
+        idle = true;
     }
     const uint32_t lo = kb + split * a.chunk;
-    const uint32_t hi = n_keys ? min(lo + a.chunk, ke) : lo;
-    const bool has_new = n_keys && pos_new >= lo && pos_new < hi;
+    const uint32_t hi = (n_keys && !idle) ? min(lo + a.chunk, ke) : lo;
+    const bool has_new = n_keys && !idle && pos_new >= lo && pos_new < hi;
     const uint32_t cache_hi = has_new ? pos_new : hi;
     const uint32_t n_cached = cache_hi > lo ? cache_hi - lo : 0;
-    const uint32_t n_stages = (n_cached + kStagePos - 1) / kStagePos;
+    const uint32_t n_stages = (n_cached + SP - 1) / SP;
+    const uint32_t n_wait = max(n_stages, spec_rows ? 1u : 0u);  // stages whose copies land here
 
-    const uint64_t head_base =
-        (static_cast<uint64_t>(b) * a.kv_heads + kvh) * a.capacity * kD;  // element offset
     const uint16_t *kc = a.k_cache + head_base + static_cast<uint64_t>(lo - a.kv_begin) * kD;
     const uint16_t *vc = a.v_cache + head_base + static_cast<uint64_t>(lo - a.kv_begin) * kD;
 
-    if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(smem_u32(&sm.full[s]), 1);
-            mbar_init(smem_u32(&sm.empty[s]), kConsumerWarps);
-        }
-        fence_mbar_init();
-    }
-    __syncthreads();
-
-    if (warp == kConsumerWarps) {
+    if (warp == CW) {
         // ---------------------------------------------------------------- producer
         if (lane == 0) {
-            for (uint32_t s = 0; s < n_stages; ++s) {
-                const uint32_t slot = s % kStages;
-                if (s >= kStages && !mbar_wait(smem_u32(&sm.empty[slot]), ((s / kStages) - 1) & 1, a.status))
-                    break;
-                const uint32_t p0 = s * kStagePos;
-                const uint32_t n = min(static_cast<uint32_t>(kStagePos), n_cached - p0);
+            for (uint32_t s = spec_rows ? 1u : 0u; s < n_stages; ++s) {
+                const uint32_t slot = s % ST;
+                if (s >= ST && !mbar_wait(smem_u32(&sm.empty[slot]), ((s / ST) - 1) & 1, a.status)) break;
+                const uint32_t p0 = s * SP;
+                const uint32_t n = min(static_cast<uint32_t>(SP), n_cached - p0);
                 const uint32_t bytes = n * kRowBytes;
                 const uint32_t full = smem_u32(&sm.full[slot]);
                 mbar_arrive_expect_tx(full, 2 * bytes);
                 tma_bulk_load(smem_u32(sm.k[slot]), kc + static_cast<uint64_t>(p0) * kD, bytes, full);
                 tma_bulk_load(smem_u32(sm.v[slot]), vc + static_cast<uint64_t>(p0) * kD, bytes, full);
             }
+        }
+        if constexpr (CL) {  // both cluster barrier phases, like every thread of the cluster
+            cluster_wait_acquire();
+            cluster_arrive_relaxed();
+            cluster_wait_acquire();
         }
         return;
     }
@@ -379,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
     // This warp's row (q of head kvh*G + warp for warps 0..G-1; the new k / v for warps G, G+1 of
     // the split that owns the new position) and its norm weights are loaded first, so their latency
     // overlaps the cos/sin table below.
-    const bool row_q = warp < kG, row_kv = !row_q && has_new, is_k = warp == kG;
+    const bool row_q = warp < kG, row_kv = warp >= kG && warp < kG + 2 && has_new, is_k = warp == kG;
     uint4 raw = make_uint4(0u, 0u, 0u, 0u);
     float wv[8];
     {
@@ -393,9 +475,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
     }
     // cos/sin of the new position, one pair per consumer thread
     const float pos_f = static_cast<float>(pos_new);
-    for (uint32_t i = tid; i < a.rope_pairs; i += kConsumerWarps * 32)
+    for (uint32_t i = tid; i < a.rope_pairs; i += CW * 32)
         rope_sincos(pos_f * a.rope.inv_freq[i], sm.rope_sn[i], sm.rope_cs[i]);
-    consumer_sync();
+    consumer_sync<CW>();
     if (row_q) {
         // q: norm + rope at the new position, pre-scaled for exp2
         float x[8];
@@ -418,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
                         static_cast<uint64_t>(pos_new - a.kv_begin) * kD;
         *reinterpret_cast<uint4 *>(dst + 8 * lane) = packed;
     }
-    consumer_sync();
+    consumer_sync<CW>();
 
     float qf[kG][8];
 #pragma unroll
@@ -434,10 +516,10 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
 
-    for (uint32_t s = 0; s < n_stages; ++s) {
-        const uint32_t slot = s % kStages;
-        if (!mbar_wait(smem_u32(&sm.full[slot]), (s / kStages) & 1, a.status)) break;
-        const int n = static_cast<int>(min(static_cast<uint32_t>(kStagePos), n_cached - s * kStagePos));
+    for (uint32_t s = 0; s < n_wait; ++s) {
+        const uint32_t slot = s % ST;
+        if (!mbar_wait(smem_u32(&sm.full[slot]), (s / ST) & 1, a.status)) break;
+        const int n = s < n_stages ? static_cast<int>(min(static_cast<uint32_t>(SP), n_cached - s * SP)) : 0;
         const int nvalid = min(max(n - static_cast<int>(warp) * kPosPerWarp, 0), kPosPerWarp);
         if (nvalid > 0)
             warp_step(sm.k[slot] + warp * kPosPerWarp * kRowBytes,
@@ -456,8 +538,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
     lt += __shfl_xor_sync(0xffffffffu, lt, 16);
     const float lother = __shfl_xor_sync(0xffffffffu, lt, 2);
     const int my_g = (lane >> 1) & 1;
-    consumer_sync();  // every warp is done with the stage buffers: reuse them for the merge
-    float *wacc = reinterpret_cast<float *>(sm.k[0]);  // [warps][G][D] f32 = 8 KB
+    consumer_sync<CW>();  // every warp is done with the stage buffers: reuse them for the merge
+    float *wacc = reinterpret_cast<float *>(sm.k[0]);  // [warps][G][D] f32
     if (lane == 0) {
         sm.wm[warp][0] = m[0];
         sm.wm[warp][1] = m[1];
@@ -468,144 +550,186 @@ __global__ void __launch_bounds__(kThreads, 2) decode_splitkv_kernel(const __gri
     for (int g = 0; g < kG; ++g)
 #pragma unroll
         for (int e = 0; e < 8; ++e) wacc[(warp * kG + g) * kD + 8 * lane + e] = acc[g][e];
-    consumer_sync();
+    consumer_sync<CW>();
 
-    // ---- CTA merge: thread t owns head g = t / 64, dims [4*(t%64), +4)
-    const uint32_t g = tid / 64, d0 = (tid % 64) * 4;
+    // ---- CTA merge: thread t owns head g, dims [d0, d0 + DPT)
+    const uint32_t g = tid / (kD / DPT), d0 = (tid % (kD / DPT)) * DPT;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w)
+    for (int w = 0; w < CW; ++w)
         if (sm.wl[w][g] > 0.f) M = fmaxf(M, sm.wm[w][g]);
-    float den = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+    float den = 0.f, o[DPT];
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) {
+    for (int e = 0; e < DPT; ++e) o[e] = 0.f;
+#pragma unroll
+    for (int w = 0; w < CW; ++w) {
         if (!(sm.wl[w][g] > 0.f)) continue;
         const float wt = fast_exp2(sm.wm[w][g] - M);
         den += wt * sm.wl[w][g];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) o[e] += wt * wacc[(w * kG + g) * kD + d0 + e];
+        for (int e = 0; e < DPT; ++e) o[e] += wt * wacc[(w * kG + g) * kD + d0 + e];
     }
     const float inv_den = den > 0.f ? 1.0f / den : 0.f;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) o[e] *= inv_den;
+    for (int e = 0; e < DPT; ++e) o[e] *= inv_den;
     const uint32_t h = kvh * kG + g;
     const uint64_t row = static_cast<uint64_t>(b) * Hq + h;
 
-    if (nsplit == 1) {
+    if constexpr (CL) {
+        // ---- push this split's partial into the leader's shared memory (counted on its barrier)
+        cluster_wait_acquire();  // the leader's barrier and buffer are initialised
+        const uint32_t leader_rec = mapa(smem_u32(&sm.parts[split][g][0]), 0);
+        const uint32_t leader_bar = mapa(smem_u32(&sm.gather), 0);
+        st_async_f32x2(leader_rec + d0 * 4, o[0], o[1], leader_bar);
+        if (d0 == 0) st_async_f32x2(leader_rec + kD * 4, M, den, leader_bar);
+        // The second cluster barrier phase keeps every CTA resident until the leader has merged
+        // (so the pushes of a CTA that is done have certainly landed before it exits).
+        if (split != 0 || !mbar_wait_cluster(smem_u32(&sm.gather), 0, a.status)) {
+            cluster_arrive_relaxed();
+            cluster_wait_acquire();
+            return;
+        }
+        // ---- leader: log-sum-exp merge of the cluster's partials
+        float Mx = -INFINITY;
+        for (uint32_t s = 0; s < gridDim.x; ++s) {
+            const float *p = sm.parts[s][g];
+            if (p[kD + 1] > 0.f) Mx = fmaxf(Mx, p[kD]);
+        }
+        float dt = 0.f, r[DPT];
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) r[e] = 0.f;
+        for (uint32_t s = 0; s < gridDim.x; ++s) {
+            const float *p = sm.parts[s][g];
+            if (!(p[kD + 1] > 0.f)) continue;
+            const float wt = fast_exp2(p[kD] - Mx) * p[kD + 1];
+            dt += wt;
+#pragma unroll
+            for (int e = 0; e < DPT; ++e) r[e] += wt * p[d0 + e];
+        }
+        const float inv = dt > 0.f ? 1.0f / dt : 0.f;
+#pragma unroll
+        for (int e = 0; e < DPT; e += 2)
+            *reinterpret_cast<uint32_t *>(a.out + row * kD + d0 + e) = pack_bf16(r[e] * inv, r[e + 1] * inv);
+        cluster_arrive_relaxed();
+        cluster_wait_acquire();
+        return;
+    } else {
+        if (nsplit == 1) {
+            if (a.peer_mode) {
+                peer_publish_merge(a, sm, b, kvh, tid, g, d0, o, M, den);
+            } else if (a.partial_mode) {
+                float *dst = a.partial_out + row * kPart;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dst[d0 + e] = o[e];
+                if (d0 == 0) {
+                    dst[kD] = M;
+                    dst[kD + 1] = den;
+                }
+            } else {
+                uint2 packed;
+                packed.x = pack_bf16(o[0], o[1]);
+                packed.y = pack_bf16(o[2], o[3]);
+                *reinterpret_cast<uint2 *>(a.out + row * kD + d0) = packed;
+            }
+            return;
+        }
+
+        // ---- split partial -> workspace; the last CTA of (b, kv head) merges all splits
+        float *mine = a.ws_part + (row * a.max_splits + split) * kWsRec;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) mine[d0 + e] = o[e];
+        if (d0 == 0) {
+            mine[kD] = M;
+            mine[kD + 1] = den;
+        }
+        consumer_sync();
+        if (tid == 0) {
+            // the barrier orders every consumer's partial before this thread's release fence, which
+            // then publishes them all to the CTA that sees the count complete
+            __threadfence();
+            unsigned *counter = a.ws_count + static_cast<uint64_t>(b) * a.kv_heads + kvh;
+            const unsigned prev = atomicAdd(counter, 1u);
+            const int last = prev == nsplit - 1;
+            if (last) *counter = 0;  // ready for the next call
+            sm.is_last = last;
+        }
+        consumer_sync();
+        if (!sm.is_last) return;
+        __threadfence();
+        // Parallel log-sum-exp merge of the nsplit partials of both heads: per-split (m, l) staged in
+        // shared memory (the stage buffers are free), block reductions for the max and the sum,
+        // then each thread accumulates its 4 dims over the splits with independent 16-byte loads.
+        const float *parts0 = a.ws_part + (static_cast<uint64_t>(b) * Hq + kvh * kG) * a.max_splits * kWsRec;
+        float *ms = reinterpret_cast<float *>(sm.v[0]);  // [G][nsplit] m, then the weights
+        float *ls = ms + kG * nsplit;                      // [G][nsplit] l
+        float mx[kG] = {-INFINITY, -INFINITY};
+        for (uint32_t s = tid; s < nsplit; s += kConsumerWarps * 32) {
+#pragma unroll
+            for (int gg = 0; gg < kG; ++gg) {
+                const float *p = parts0 + (static_cast<uint64_t>(gg) * a.max_splits + s) * kWsRec;
+                const float2 ml = __ldcg(reinterpret_cast<const float2 *>(p + kD));
+                ms[gg * nsplit + s] = ml.x;
+                ls[gg * nsplit + s] = ml.y;
+                if (ml.y > 0.f) mx[gg] = fmaxf(mx[gg], ml.x);
+            }
+        }
+        consumer_reduce<true>(mx, sm.red, warp, lane);
+        float dsum[kG] = {0.f, 0.f};
+        for (uint32_t s = tid; s < nsplit; s += kConsumerWarps * 32) {
+#pragma unroll
+            for (int gg = 0; gg < kG; ++gg) {
+                const float l_s = ls[gg * nsplit + s];
+                const float wt = l_s > 0.f ? fast_exp2(ms[gg * nsplit + s] - mx[gg]) * l_s : 0.f;
+                ms[gg * nsplit + s] = wt;
+                dsum[gg] += wt;
+            }
+        }
+        consumer_reduce<false>(dsum, sm.red, warp, lane);  // its barriers also publish the weights
+        const float *pg = parts0 + static_cast<uint64_t>(g) * a.max_splits * kWsRec + d0;
+        const float *wg = ms + g * nsplit;
+        float r[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t s = 0;
+        for (; s + 8 <= nsplit; s += 8) {  // 8 independent 16-byte loads in flight per thread
+            float4 ov[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) ov[u] = __ldcg(reinterpret_cast<const float4 *>(pg + (s + u) * kWsRec));
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float wt = wg[s + u];
+                r[0] += wt * ov[u].x;
+                r[1] += wt * ov[u].y;
+                r[2] += wt * ov[u].z;
+                r[3] += wt * ov[u].w;
+            }
+        }
+        for (; s < nsplit; ++s) {
+            const float4 ov = __ldcg(reinterpret_cast<const float4 *>(pg + s * kWsRec));
+            const float wt = wg[s];
+            r[0] += wt * ov.x;
+            r[1] += wt * ov.y;
+            r[2] += wt * ov.z;
+            r[3] += wt * ov.w;
+        }
+        const float Mx = mx[g], dtot = dsum[g];
+        const float inv = dtot > 0.f ? 1.0f / dtot : 0.f;
         if (a.peer_mode) {
-            peer_publish_merge(a, sm, b, kvh, tid, g, d0, o, M, den);
+            const float on[4] = {r[0] * inv, r[1] * inv, r[2] * inv, r[3] * inv};
+            peer_publish_merge(a, sm, b, kvh, tid, g, d0, on, Mx, dtot);
         } else if (a.partial_mode) {
+            // A rank partial stores l relative to its own max Mx: l_rank = sum_s 2^(m_s - Mx) l_s.
             float *dst = a.partial_out + row * kPart;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) dst[d0 + e] = o[e];
+            for (int e = 0; e < 4; ++e) dst[d0 + e] = r[e] * inv;
             if (d0 == 0) {
-                dst[kD] = M;
-                dst[kD + 1] = den;
+                dst[kD] = Mx;
+                dst[kD + 1] = dtot;
             }
         } else {
             uint2 packed;
-            packed.x = pack_bf16(o[0], o[1]);
-            packed.y = pack_bf16(o[2], o[3]);
+            packed.x = pack_bf16(r[0] * inv, r[1] * inv);
+            packed.y = pack_bf16(r[2] * inv, r[3] * inv);
             *reinterpret_cast<uint2 *>(a.out + row * kD + d0) = packed;
         }
-        return;
-    }
-
-    // ---- split partial -> workspace; the last CTA of (b, kv head) merges all splits
-    float *mine = a.ws_part + (row * a.max_splits + split) * kWsRec;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) mine[d0 + e] = o[e];
-    if (d0 == 0) {
-        mine[kD] = M;
-        mine[kD + 1] = den;
-    }
-    consumer_sync();
-    if (tid == 0) {
-        // the barrier orders every consumer's partial before this thread's release fence, which
-        // then publishes them all to the CTA that sees the count complete
-        __threadfence();
-        unsigned *counter = a.ws_count + static_cast<uint64_t>(b) * a.kv_heads + kvh;
-        const unsigned prev = atomicAdd(counter, 1u);
-        const int last = prev == nsplit - 1;
-        if (last) *counter = 0;  // ready for the next call
-        sm.is_last = last;
-    }
-    consumer_sync();
-    if (!sm.is_last) return;
-    __threadfence();
-    // Parallel log-sum-exp merge of the nsplit partials of both heads: per-split (m, l) staged in
-    // shared memory (the stage buffers are free), block reductions for the max and the sum,
-    // then each thread accumulates its 4 dims over the splits with independent 16-byte loads.
-    const float *parts0 = a.ws_part + (static_cast<uint64_t>(b) * Hq + kvh * kG) * a.max_splits * kWsRec;
-    float *ms = reinterpret_cast<float *>(sm.v[0]);  // [G][nsplit] m, then the weights
-    float *ls = ms + kG * nsplit;                      // [G][nsplit] l
-    float mx[kG] = {-INFINITY, -INFINITY};
-    for (uint32_t s = tid; s < nsplit; s += kConsumerWarps * 32) {
-#pragma unroll
-        for (int gg = 0; gg < kG; ++gg) {
-            const float *p = parts0 + (static_cast<uint64_t>(gg) * a.max_splits + s) * kWsRec;
-            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(p + kD));
-            ms[gg * nsplit + s] = ml.x;
-            ls[gg * nsplit + s] = ml.y;
-            if (ml.y > 0.f) mx[gg] = fmaxf(mx[gg], ml.x);
-        }
-    }
-    consumer_reduce<true>(mx, sm.red, warp, lane);
-    float dsum[kG] = {0.f, 0.f};
-    for (uint32_t s = tid; s < nsplit; s += kConsumerWarps * 32) {
-#pragma unroll
-        for (int gg = 0; gg < kG; ++gg) {
-            const float l_s = ls[gg * nsplit + s];
-            const float wt = l_s > 0.f ? fast_exp2(ms[gg * nsplit + s] - mx[gg]) * l_s : 0.f;
-            ms[gg * nsplit + s] = wt;
-            dsum[gg] += wt;
-        }
-    }
-    consumer_reduce<false>(dsum, sm.red, warp, lane);  // its barriers also publish the weights
-    const float *pg = parts0 + static_cast<uint64_t>(g) * a.max_splits * kWsRec + d0;
-    const float *wg = ms + g * nsplit;
-    float r[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t s = 0;
-    for (; s + 8 <= nsplit; s += 8) {  // 8 independent 16-byte loads in flight per thread
-        float4 ov[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) ov[u] = __ldcg(reinterpret_cast<const float4 *>(pg + (s + u) * kWsRec));
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const float wt = wg[s + u];
-            r[0] += wt * ov[u].x;
-            r[1] += wt * ov[u].y;
-            r[2] += wt * ov[u].z;
-            r[3] += wt * ov[u].w;
-        }
-    }
-    for (; s < nsplit; ++s) {
-        const float4 ov = __ldcg(reinterpret_cast<const float4 *>(pg + s * kWsRec));
-        const float wt = wg[s];
-        r[0] += wt * ov.x;
-        r[1] += wt * ov.y;
-        r[2] += wt * ov.z;
-        r[3] += wt * ov.w;
-    }
-    const float Mx = mx[g], dtot = dsum[g];
-    const float inv = dtot > 0.f ? 1.0f / dtot : 0.f;
-    if (a.peer_mode) {
-        const float on[4] = {r[0] * inv, r[1] * inv, r[2] * inv, r[3] * inv};
-        peer_publish_merge(a, sm, b, kvh, tid, g, d0, on, Mx, dtot);
-    } else if (a.partial_mode) {
-        // A rank partial stores l relative to its own max Mx: l_rank = sum_s 2^(m_s - Mx) l_s.
-        float *dst = a.partial_out + row * kPart;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) dst[d0 + e] = r[e] * inv;
-        if (d0 == 0) {
-            dst[kD] = Mx;
-            dst[kD + 1] = dtot;
-        }
-    } else {
-        uint2 packed;
-        packed.x = pack_bf16(r[0] * inv, r[1] * inv);
-        packed.y = pack_bf16(r[2] * inv, r[3] * inv);
-        *reinterpret_cast<uint2 *>(a.out + row * kD + d0) = packed;
     }
 }
 
@@ -681,12 +805,90 @@ int check_params(const apex_attn_params *p, const char *name) {
     return APEX_OK;
 }
 
-// A validated decode launch: arguments and grid, or empty (batch 0: nothing to launch).
+// A validated decode launch: arguments and grid, or empty (batch 0: nothing to launch).  cluster > 0
+// selects the cluster form (grid.x == cluster CTAs per (sequence, kv head)).
 struct DecodePlan {
     DecodeArgs a{};
     dim3 grid;
+    uint32_t cluster = 0;
+    int stages = 0;  // cluster form: ring stages (1 or 2)
     bool empty = false;
 };
+
+using ShortSmem1 = DecodeSmemT<kShortWarps, 1, true>;
+using ShortSmem2 = DecodeSmemT<kShortWarps, 2, true>;
+
+template <int ST>
+size_t short_smem_bytes() { return ST == 1 ? sizeof(ShortSmem1) : sizeof(ShortSmem2); }
+
+// How many clusters of `size` CTAs of the cluster form (ring of ST stages) can be resident at once
+// on the current device; sets the kernel's attributes first (once per device).
+template <int ST>
+int active_clusters(uint32_t size) {
+    static std::mutex mu;
+    static std::vector<std::vector<int>> cache;  // [device][size]: -1 unknown
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1);
+    auto &row = cache[dev];
+    if (row.empty()) {
+        auto *kernel = decode_kernel<kShortWarps, ST, true>;
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(short_smem_bytes<ST>())) != cudaSuccess ||
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+            cudaGetLastError();
+            row.assign(kMaxCluster + 1, 0);
+            return 0;
+        }
+        row.assign(kMaxCluster + 1, -1);
+    }
+    if (row[size] < 0) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(size, 1, 1);
+        cfg.blockDim = dim3((kShortWarps + 1) * 32, 1, 1);
+        cfg.dynamicSmemBytes = short_smem_bytes<ST>();
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = size;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, decode_kernel<kShortWarps, ST, true>, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        row[size] = n;
+    }
+    return row[size];
+}
+
+// Cluster size for a short-context decode of `batch` sequences, or 0 for the split-KV form.  The
+// cluster form is taken when every (sequence, kv head) gets a cluster of at least two splits and
+// all the clusters are resident at once (one wave); at short contexts the step is latency, and
+// merging in distributed shared memory saves the workspace round trip and the second pass.  Splits
+// of one 64-position stage use a one-stage ring (about 100 KB of shared memory, two CTAs per SM).
+uint32_t short_cluster(uint32_t batch, uint32_t kv_heads, uint32_t range_len, uint32_t &chunk, int &stages) {
+    const uint64_t pairs = static_cast<uint64_t>(batch) * kv_heads;
+    const uint64_t most = std::min<uint64_t>(kMaxCluster, (range_len + kShortStagePos - 1) / kShortStagePos);
+    for (uint64_t c = most; c >= 2; --c) {
+        uint64_t ch = (range_len + c - 1) / c;
+        ch = (ch + kShortStagePos - 1) / kShortStagePos * kShortStagePos;
+        const uint64_t used = (range_len + ch - 1) / ch;
+        if (used < 2 || used != c) continue;
+        const int st = ch == kShortStagePos ? 1 : 2;
+        const int fit = st == 1 ? active_clusters<1>(static_cast<uint32_t>(used))
+                                : active_clusters<2>(static_cast<uint32_t>(used));
+        if (static_cast<uint64_t>(fit) >= pairs) {
+            chunk = static_cast<uint32_t>(ch);
+            stages = st;
+            return static_cast<uint32_t>(used);
+        }
+    }
+    return 0;
+}
 
 // Checks every argument of a decode call and fills `plan`; queues nothing.
 int plan_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t *k_new,
@@ -764,9 +966,20 @@ int plan_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t
     rope_table(a.rope.inv_freq, p->rope_pairs, kD, p->rope_base);
     a.status = device_status_ptr();
     if (!a.status) return fail(APEX_ERR_CUDA, std::string(name) + ": device status word unavailable");
-    const uint32_t grid_x = std::max<uint32_t>(1, (std::max<uint32_t>(range_len, 1) + a.chunk - 1) / a.chunk);
+    uint32_t grid_x = std::max<uint32_t>(1, (std::max<uint32_t>(range_len, 1) + a.chunk - 1) / a.chunk);
     if (grid_x > max_splits)
         return fail(APEX_ERR_WORKSPACE, std::string(name) + ": internal split plan exceeds workspace");
+    if (!partial_mode && !peer && max_seq_len <= kShortMaxLen) {
+        uint32_t chunk = 0;
+        int stages = 0;
+        const uint32_t c = short_cluster(batch, p->kv_heads, range_len, chunk, stages);
+        if (c) {
+            a.chunk = chunk;
+            grid_x = c;
+            plan.cluster = c;
+            plan.stages = stages;
+        }
+    }
     plan.grid = dim3(grid_x, p->kv_heads, batch);
     return APEX_OK;
 }
@@ -774,18 +987,37 @@ int plan_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t
 // Queues the planned decode kernel on `stream`.
 int run_decode_plan(const DecodePlan &plan, void *stream, const char *name) {
     if (plan.empty) return ok();
+    if (plan.cluster) {  // attributes were set when the plan was made (active_clusters)
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = plan.grid;
+        cfg.blockDim = dim3((kShortWarps + 1) * 32, 1, 1);
+        cfg.dynamicSmemBytes = plan.stages == 1 ? short_smem_bytes<1>() : short_smem_bytes<2>();
+        cfg.stream = static_cast<cudaStream_t>(stream);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = plan.cluster;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const int rc = check_cuda(plan.stages == 1
+                                      ? cudaLaunchKernelEx(&cfg, decode_kernel<kShortWarps, 1, true>, plan.a)
+                                      : cudaLaunchKernelEx(&cfg, decode_kernel<kShortWarps, 2, true>, plan.a),
+                                  name);
+        return rc ? rc : ok();
+    }
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
+    auto *kernel = decode_kernel<kConsumerWarps, kStages, false>;
     if (dev < 64 && !attr_set[dev]) {
-        const int rc = check_cuda(cudaFuncSetAttribute(decode_splitkv_kernel,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+        const int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                        static_cast<int>(sizeof(DecodeSmem))),
                                   "decode smem attribute");
         if (rc) return rc;
         attr_set[dev] = true;
     }
-    decode_splitkv_kernel<<<plan.grid, kThreads, sizeof(DecodeSmem), static_cast<cudaStream_t>(stream)>>>(plan.a);
+    kernel<<<plan.grid, kThreads, sizeof(DecodeSmem), static_cast<cudaStream_t>(stream)>>>(plan.a);
     const int rc = check_cuda(cudaGetLastError(), name);
     return rc ? rc : ok();
 }

@@ -380,7 +380,7 @@ class DecodeWorkload:
         owns_tokens = not self.kv_split or rank == 0
         self.tokens = B if owns_tokens else 0
         self.launches_per_step = 2 if self.kv_split and self.peer is None else 1
-        self.kernel_name = "decode_splitkv_kernel" + (" (partial mode, this rank's key range)" if self.kv_split else "")
+        self.kernel_name = "decode_kernel" + (" (partial mode, this rank's key range)" if self.kv_split else "")
 
     def _call(self, s):
         if self.peer is not None:

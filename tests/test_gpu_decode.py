@@ -94,6 +94,22 @@ def test_decode_edge_lengths(window):
         assert_close(got[i], ref, f"L={L} window={window}")
 
 
+@pytest.mark.parametrize("window", [0, 64])
+def test_short_context_cluster_form(window):
+    """Small batches at contexts up to 4096 take the cluster form (one thread-block cluster per
+    (sequence, kv head), partials merged in the leader CTA's shared memory): one split up to 16,
+    splits of several stages, and a ragged batch whose short sequences leave splits idle."""
+    cfg = dataclasses.replace(CONFIGS["c1_decode"], window=window, seed=31)
+    for lens in ([1], [2], [63], [64], [65], [130], [500], [1000], [1024], [1025], [2047], [4096], [100, 1024, 7]):
+        shape, t = build_decode(cfg, list(range(len(lens))), lens, cap=max(lens))
+        got, ws = run_decode(shape, t)
+        again, _ = run_decode(shape, t, ws)
+        np.testing.assert_array_equal(got, again)
+        for i, L in enumerate(lens):
+            ref, _, _ = oracle_decode_seq(cfg, i, L)
+            assert_close(got[i], ref, f"L={L} window={window}")
+
+
 def test_decode_repeated_calls_are_identical():
     cfg = dataclasses.replace(CONFIGS["c3_ragged_decode"], batch=6, seed=22)
     lens = [5000, 700, 8192, 513, 3000, 6001]
