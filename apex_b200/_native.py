@@ -31,6 +31,8 @@ EXPORTED = (
     "apex_attn_prefill_prep_bf16", "apex_attn_prefill_attend_bf16", "apex_attn_decode_bf16_noalloc",
     "apex_attn_peer_exchange_bytes", "apex_attn_decode_kvsplit_bf16", "apex_device_alloc",
     "apex_device_free", "apex_ipc_get_handle", "apex_ipc_open_handle", "apex_ipc_close_handle",
+    "apex_matmul_nvfp4_f32", "apex_matmul_nvfp4", "apex_rms_norm_f32", "apex_matmul_nvfp4_rms_norm_workspace_bytes",
+    "apex_matmul_nvfp4_rms_norm",
     # include/apex_loader.h
     "apex_model_open", "apex_model_close", "apex_model_summary_get", "apex_model_tensor", "apex_model_expert_piece",
     "apex_model_verify", "apex_model_upload_core", "apex_model_load_expert",
@@ -117,6 +119,13 @@ def load(path: str | pathlib.Path | None = None):
     L.apex_attn_prefill_bf16.argtypes = ([_PP] + [_vp] * 7 + [_u32, _u32, _u32, _u32, _vp, _vp, _sz, _vp])
     L.apex_attn_prefill_prep_bf16.argtypes = ([_PP] + [_vp] * 7 + [_u32, _u32, _u32, _u32, _vp, _sz, _vp])
     L.apex_attn_prefill_attend_bf16.argtypes = ([_PP, _vp, _sz, _vp, _vp] + [_u32, _u32, _u32, _u32, _vp, _vp])
+    L.apex_matmul_nvfp4_f32.argtypes = [_vp] * 4 + [_u32] * 3 + [_vp]
+    L.apex_matmul_nvfp4.argtypes = [_vp, _i32, _vp, _vp, _vp, _i32, _u32, _u32, _u32, _vp]
+    L.apex_rms_norm_f32.argtypes = [_vp, _vp, _vp, _u32, _u32, _f32, _vp]
+    L.apex_matmul_nvfp4_rms_norm_workspace_bytes.argtypes = [_u32, _u32]
+    L.apex_matmul_nvfp4_rms_norm_workspace_bytes.restype = _sz
+    L.apex_matmul_nvfp4_rms_norm.argtypes = [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32, _vp, _sz,
+                                             _vp]
     _PU64 = ctypes.POINTER(ctypes.c_uint64)
     L.apex_model_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(_vp)]
     L.apex_model_close.argtypes = [_vp]
@@ -129,7 +138,8 @@ def load(path: str | pathlib.Path | None = None):
     L.apex_model_load_expert.argtypes = [_vp, _u32, _u32, _vp, _sz, _i32, _vp]
     for fn in EXPORTED:
         if fn not in ("apex_cuda_last_error", "apex_attn_decode_workspace_bytes",
-                      "apex_attn_prefill_workspace_bytes", "apex_model_close"):
+                      "apex_attn_prefill_workspace_bytes", "apex_model_close",
+                      "apex_matmul_nvfp4_rms_norm_workspace_bytes"):
             getattr(L, fn).restype = _i32
     _lib = L
     return L

@@ -182,6 +182,26 @@ void launch_merge(const std::vector<Arg> &a, Dim3 g, cudaStream_t s, const char 
                k);
 }
 
+// src/ops.h:39-44 order: input, weights(+offset), scales(+offset), output, hidden_dim, w_rows;
+// grid {row groups of 8, tokens}.
+void launch_matmul_nvfp4(const std::vector<Arg> &a, Dim3 g, cudaStream_t s, const char *k) {
+    need_args(a, 6, k);
+    const uint32_t w_rows = val<uint32_t>(a[5], k, 5);
+    if (g.x * 8 < w_rows) throw std::runtime_error(std::string(k) + ": grid.x must cover w_rows in groups of 8");
+    apex_check(apex_matmul_nvfp4_f32(ptr<const float>(a[0], k, 0), ptr<const uint32_t>(a[1], k, 1),
+                                     ptr<const uint8_t>(a[2], k, 2), ptr<float>(a[3], k, 3),
+                                     val<uint32_t>(a[4], k, 4), w_rows, g.y, s),
+               k);
+}
+
+// src/ops.h:21-26 order: input, weights(+offset), result, hidden_dim, eps; grid {rows}.
+void launch_rms_norm(const std::vector<Arg> &a, Dim3 g, cudaStream_t s, const char *k) {
+    need_args(a, 5, k);
+    apex_check(apex_rms_norm_f32(ptr<const float>(a[0], k, 0), ptr<const uint16_t>(a[1], k, 1),
+                                 ptr<float>(a[2], k, 2), g.x, val<uint32_t>(a[3], k, 3), val<float>(a[4], k, 4), s),
+               k);
+}
+
 const std::map<std::string, Launcher> &launchers() {
     static const std::map<std::string, Launcher> table = {
         {"head_norm_rope_f32", [](auto &a, Dim3 g, cudaStream_t s) { launch_head_norm_rope(a, g, s, false, "head_norm_rope_f32"); }},
@@ -190,6 +210,8 @@ const std::map<std::string, Launcher> &launchers() {
         {"attention_decode_bf16", [](auto &a, Dim3 g, cudaStream_t s) { launch_decode(a, g, s, "attention_decode_bf16"); }},
         {"attention_prefill_bf16", [](auto &a, Dim3 g, cudaStream_t s) { launch_prefill(a, g, s, "attention_prefill_bf16"); }},
         {"attention_merge_partials", [](auto &a, Dim3 g, cudaStream_t s) { launch_merge(a, g, s, "attention_merge_partials"); }},
+        {"matmul_nvfp4", [](auto &a, Dim3 g, cudaStream_t s) { launch_matmul_nvfp4(a, g, s, "matmul_nvfp4"); }},
+        {"rms_norm_f32", [](auto &a, Dim3 g, cudaStream_t s) { launch_rms_norm(a, g, s, "rms_norm_f32"); }},
     };
     return table;
 }

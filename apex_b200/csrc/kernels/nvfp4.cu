@@ -1,0 +1,560 @@
+// nvfp4.cu -- the projections either side of the attention path (NVFP4 weights) and RMSNorm.
+//
+// Reference semantics:
+//   matmul_nvfp4 (shaders/matmul.metal:4-53, launched by apex::matmulNvfp4, src/ops.h:34-46):
+//     output[t][r] = sum_g e4m3(scales[r][g]) * sum_{i<16} e2m1(code_{r,16g+i}) * input[t][16g+i]
+//     with codes uint32 [rows][n/8] (8 codes per word, low nibble first) and E4M3 scales
+//     [rows][n/16] (src/nvfp4.h:11-43; CPU form src/tests/cpu_ref.h:48-63).
+//   rms_norm_f32 (shaders/norm.metal:36-81, apex::rmsNorm, src/ops.h:18-27):
+//     y = x * rsqrt(mean(x^2) + eps) * w, w raw bf16 bits.
+//   The attention block ends with out = W_o . o and attn_out = rmsnorm(out, post_attention_norm)
+//   (docs/B6_3_attention.md:15-28); apex_matmul_nvfp4_rms_norm fuses the two.
+//
+// B200 design.  A decode projection is a matrix-vector product over a few tokens: HBM-bound on the
+// 0.5625 bytes per weight, with ~3 instructions per weight to decode, so the kernel keeps the decode
+// off the critical resources: the E2M1 pairs and the E4M3 scale go through the sm_100 hardware
+// conversions (cvt e2m1x2 -> f16x2, e4m3 -> f16; every E2M1 x E4M3 value is exact in f16 and f32),
+// each warp owns 2 weight rows so one 16-wide input chunk serves both, every lane keeps 8 groups of
+// both rows' codes (64 B) in flight, and a token chunk of 4 reuses each decoded weight 4 times.  Sums
+// are f32 (the reference's per-group partial, then scale, then a warp reduction -- its order).
+// Inputs are f32 or bf16 (the attention output), outputs f32 or bf16 (raw q/k/v for the bf16 path).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp4.h>
+#include <cuda_fp8.h>
+
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace apex {
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRowsPerWarp = 2;
+constexpr int kRowsPerCta = kWarps * kRowsPerWarp;
+constexpr int kTok = 4;         // tokens per pass over the weights
+constexpr int kBatch = 8;       // groups of 16 weights per lane in flight
+constexpr uint32_t kFusedMaxTokens = 16;  // above this the fused norm runs as a second launch
+
+struct NormEpilogue {
+    const uint16_t *weight = nullptr;  // bf16 [rows]; null = no fused norm
+    const float *residual = nullptr;   // optional [tokens][rows]
+    float *residual_out = nullptr;     // optional: residual + normalised output
+    float *ws_sumsq = nullptr;         // [ctas][tokens] per-CTA sums of squares
+    unsigned *ws_count = nullptr;      // CTAs done
+    float eps = 0.f;
+};
+
+__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
+    const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E4M3);
+    return __half2float(__half(h));
+}
+
+// 16 weights of one group: byte k of the 8 code bytes holds weights 2k (low nibble) and 2k+1.
+__device__ __forceinline__ void decode_group(uint2 c, float (&w)[16]) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t word = k < 4 ? c.x : c.y;
+        const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2(static_cast<__nv_fp4x2_storage_t>((word >> (8 * (k & 3))) & 0xFFu),
+                                                       __NV_E2M1);
+        const float2 f = __half22float2(__half2(h));
+        w[2 * k] = f.x;
+        w[2 * k + 1] = f.y;
+    }
+}
+
+__device__ __forceinline__ void load16(const float *p, float (&x)[16]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(p) + k);
+        x[4 * k] = v.x;
+        x[4 * k + 1] = v.y;
+        x[4 * k + 2] = v.z;
+        x[4 * k + 3] = v.w;
+    }
+}
+__device__ __forceinline__ void load16(const __nv_bfloat16 *p, float (&x)[16]) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p) + k);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            x[8 * k + 2 * e] = bf16lo(u[e]);
+            x[8 * k + 2 * e + 1] = bf16hi(u[e]);
+        }
+    }
+}
+
+__device__ __forceinline__ void store(float *p, float v) { *p = v; }
+__device__ __forceinline__ void store(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// One CTA = 8 warps x 2 rows.  With a fused norm (ep.weight), TOut is f32 and `out` receives the
+// normalised rows: each CTA writes its rows before the norm, its per-token sums of squares to the
+// workspace, and the last CTA to finish (atomic counter, no spinning) sums them in CTA order and
+// rescales every row.
+template <typename TIn, typename TOut>
+__global__ void __launch_bounds__(kThreads) nvfp4_matvec_kernel(const TIn *__restrict__ input,
+                                                               const uint32_t *__restrict__ codes,
+                                                               const uint8_t *__restrict__ scales,
+                                                               TOut *__restrict__ out, uint32_t tokens,
+                                                               uint32_t rows, uint32_t n, NormEpilogue ep) {
+    __shared__ float s_sq[kWarps][kFusedMaxTokens];
+    __shared__ int s_last;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t row0 = (blockIdx.x * kWarps + warp) * kRowsPerWarp;
+    const uint32_t G = n / 16, wpr = n / 8;
+    const bool fused = ep.weight != nullptr;
+    float sq[kFusedMaxTokens];
+#pragma unroll
+    for (int t = 0; t < static_cast<int>(kFusedMaxTokens); ++t) sq[t] = 0.f;
+
+    for (uint32_t t0 = 0; t0 < tokens; t0 += kTok) {
+        const uint32_t tc = min(static_cast<uint32_t>(kTok), tokens - t0);
+        float acc[kRowsPerWarp][kTok];
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r)
+#pragma unroll
+            for (int t = 0; t < kTok; ++t) acc[r][t] = 0.f;
+
+        for (uint32_t gb = 0; gb < G; gb += 32 * kBatch) {
+            // this lane's groups gb + lane + 32k: both rows' codes and scales requested together
+            uint2 cw[kBatch][kRowsPerWarp];
+            uint8_t sc[kBatch][kRowsPerWarp];
+#pragma unroll
+            for (int k = 0; k < kBatch; ++k) {
+                const uint32_t g = gb + lane + 32u * k;
+#pragma unroll
+                for (int r = 0; r < kRowsPerWarp; ++r) {
+                    const uint32_t row = row0 + r;
+                    const bool ok = g < G && row < rows;
+                    cw[k][r] = ok ? __ldg(reinterpret_cast<const uint2 *>(codes + static_cast<uint64_t>(row) * wpr) + g)
+                                  : make_uint2(0u, 0u);
+                    sc[k][r] = ok ? __ldg(scales + static_cast<uint64_t>(row) * G + g) : 0;
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kBatch; ++k) {
+                const uint32_t g = gb + lane + 32u * k;
+                if (g >= G) break;
+                float x[kTok][16];
+#pragma unroll
+                for (int t = 0; t < kTok; ++t) {
+                    if (t < static_cast<int>(tc)) {
+                        load16(input + static_cast<uint64_t>(t0 + t) * n + 16u * g, x[t]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) x[t][j] = 0.f;
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < kRowsPerWarp; ++r) {
+                    float w[16];
+                    decode_group(cw[k][r], w);
+                    const float s = e4m3_to_f32(sc[k][r]);
+#pragma unroll
+                    for (int t = 0; t < kTok; ++t) {
+                        float part = 0.f;  // the reference's order: weights j and 8 + j in turn
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            part = fmaf(w[j], x[t][j], part);
+                            part = fmaf(w[8 + j], x[t][8 + j], part);
+                        }
+                        acc[r][t] = fmaf(s, part, acc[r][t]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) {
+            const uint32_t row = row0 + r;
+#pragma unroll
+            for (int t = 0; t < kTok; ++t) {
+                const float v = warp_sum(acc[r][t]);
+                if (row < rows && t < static_cast<int>(tc)) {
+                    if (lane == 0) store(out + static_cast<uint64_t>(t0 + t) * rows + row, v);
+                    if (fused) sq[t0 + t] += v * v;  // t0 + t < kFusedMaxTokens when fused
+                }
+            }
+        }
+    }
+    if (!fused) return;
+
+    // ---- fused RMSNorm epilogue (tokens <= kFusedMaxTokens; TOut is float)
+    if (lane == 0)
+        for (uint32_t t = 0; t < tokens; ++t) s_sq[warp][t] = sq[t];
+    __syncthreads();
+    if (threadIdx.x < tokens) {
+        float v = 0.f;
+        for (int w = 0; w < kWarps; ++w) v += s_sq[w][threadIdx.x];
+        ep.ws_sumsq[static_cast<uint64_t>(blockIdx.x) * tokens + threadIdx.x] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();  // this CTA's rows and partial sums before its count
+        const unsigned prev = atomicAdd(ep.ws_count, 1u);
+        s_last = prev == gridDim.x - 1;
+        if (s_last) *ep.ws_count = 0;  // ready for the next call
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    __shared__ float s_inv[kFusedMaxTokens];
+    if (threadIdx.x < tokens) {
+        float total = 0.f;  // CTA order: the same sum on every run
+        for (uint32_t c = 0; c < gridDim.x; ++c) total += __ldcg(ep.ws_sumsq + static_cast<uint64_t>(c) * tokens + threadIdx.x);
+        s_inv[threadIdx.x] = rsqrtf(total / static_cast<float>(rows) + ep.eps);
+    }
+    __syncthreads();
+    float *o = reinterpret_cast<float *>(out);
+    for (uint64_t i = threadIdx.x; i < static_cast<uint64_t>(tokens) * rows; i += kThreads) {
+        const uint32_t t = static_cast<uint32_t>(i / rows), r = static_cast<uint32_t>(i % rows);
+        const float y = __ldcg(o + i) * s_inv[t] * __uint_as_float(static_cast<uint32_t>(ep.weight[r]) << 16);
+        o[i] = y;
+        if (ep.residual_out) ep.residual_out[i] = (ep.residual ? ep.residual[i] : 0.f) + y;
+    }
+}
+
+// The streaming form: a persistent grid of CTAs, each walking 16-row tiles of the matrix.  One
+// producer warp copies a tile's codes and scales (each one contiguous run: the rows of a tile are
+// adjacent) into a ring of shared-memory stages with 1-D TMA bulk copies; eight consumer warps take
+// two rows each, decode from shared memory and accumulate.  The ring keeps 2-4 tiles (50-150 KB)
+// in flight per CTA without holding them in registers.
+constexpr int kTileRows = 16;
+constexpr int kMaxStages = 4;
+constexpr uint32_t kStageBudget = 200u * 1024u;
+
+struct TileArgs {
+    uint32_t tokens, rows, n, tiles, stages;
+    uint32_t code_bytes, scale_bytes, stage_bytes;  // per tile / per stage
+    unsigned *status;
+};
+
+template <typename TIn, typename TOut, int TK>
+__global__ void __launch_bounds__(kThreads + 32, TK == 1 ? 2 : 1) nvfp4_stream_kernel(const TIn *__restrict__ input,
+                                                                        const uint32_t *__restrict__ codes,
+                                                                        const uint8_t *__restrict__ scales,
+                                                                        TOut *__restrict__ out, const TileArgs ta,
+                                                                        NormEpilogue ep) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t full[kMaxStages], empty[kMaxStages];
+    __shared__ float s_sq[kWarps][kFusedMaxTokens];
+    __shared__ int s_last;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t n = ta.n, G = n / 16;
+    const bool fused = ep.weight != nullptr;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < ta.stages; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), kWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kWarps) {  // ------------------------------------------------ producer
+        if (lane == 0) {
+            uint32_t k = 0;
+            for (uint32_t tile = blockIdx.x; tile < ta.tiles; tile += gridDim.x, ++k) {
+                const uint32_t slot = k % ta.stages;
+                if (k >= ta.stages && !mbar_wait(smem_u32(&empty[slot]), ((k / ta.stages) - 1) & 1, ta.status)) break;
+                const uint32_t nrows = min(static_cast<uint32_t>(kTileRows), ta.rows - tile * kTileRows);
+                const uint32_t cb = nrows * (n / 2), sb = nrows * G;
+                uint8_t *st = smem + static_cast<size_t>(slot) * ta.stage_bytes;
+                const uint32_t fb = smem_u32(&full[slot]);
+                // both runs are multiples of 16 bytes at 16-byte offsets (the host checks n and rows)
+                mbar_arrive_expect_tx(fb, cb + sb);
+                tma_bulk_load(smem_u32(st), reinterpret_cast<const uint8_t *>(codes) + static_cast<uint64_t>(tile) * ta.code_bytes,
+                              cb, fb);
+                tma_bulk_load(smem_u32(st + ta.code_bytes), scales + static_cast<uint64_t>(tile) * ta.scale_bytes, sb, fb);
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------------- consumers
+    float sq[kFusedMaxTokens];
+#pragma unroll
+    for (int t = 0; t < static_cast<int>(kFusedMaxTokens); ++t) sq[t] = 0.f;
+    uint32_t k = 0;
+    for (uint32_t tile = blockIdx.x; tile < ta.tiles; tile += gridDim.x, ++k) {
+        const uint32_t slot = k % ta.stages;
+        if (!mbar_wait(smem_u32(&full[slot]), (k / ta.stages) & 1, ta.status)) break;
+        const uint8_t *st = smem + static_cast<size_t>(slot) * ta.stage_bytes;
+        const uint32_t rbase = tile * kTileRows;
+        const uint32_t lr0 = warp * kRowsPerWarp;  // rows lr0, lr0+1 of the tile
+        for (uint32_t t0 = 0; t0 < ta.tokens; t0 += TK) {
+            const uint32_t tc = min(static_cast<uint32_t>(TK), ta.tokens - t0);
+            float acc[kRowsPerWarp][TK];
+#pragma unroll
+            for (int r = 0; r < kRowsPerWarp; ++r)
+#pragma unroll
+                for (int t = 0; t < TK; ++t) acc[r][t] = 0.f;
+            for (uint32_t g = lane; g < G; g += 32) {
+                float x[TK][16];
+#pragma unroll
+                for (int t = 0; t < TK; ++t) {
+                    if (t < static_cast<int>(tc)) {
+                        load16(input + static_cast<uint64_t>(t0 + t) * n + 16u * g, x[t]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) x[t][j] = 0.f;
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < kRowsPerWarp; ++r) {
+                    const uint32_t lr = lr0 + r;
+                    if (rbase + lr >= ta.rows) break;
+                    const uint2 cw = *reinterpret_cast<const uint2 *>(st + static_cast<size_t>(lr) * (n / 2) + 8u * g);
+                    const float s = e4m3_to_f32(st[ta.code_bytes + static_cast<size_t>(lr) * G + g]);
+                    float w[16];
+                    decode_group(cw, w);
+#pragma unroll
+                    for (int t = 0; t < TK; ++t) {
+                        float part = 0.f;  // the reference's order: weights j and 8 + j in turn
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            part = fmaf(w[j], x[t][j], part);
+                            part = fmaf(w[8 + j], x[t][8 + j], part);
+                        }
+                        acc[r][t] = fmaf(s, part, acc[r][t]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kRowsPerWarp; ++r) {
+                const uint32_t row = rbase + lr0 + r;
+#pragma unroll
+                for (int t = 0; t < TK; ++t) {
+                    const float v = warp_sum(acc[r][t]);
+                    if (row < ta.rows && t < static_cast<int>(tc)) {
+                        if (lane == 0) store(out + static_cast<uint64_t>(t0 + t) * ta.rows + row, v);
+                        if (fused) sq[t0 + t] += v * v;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty[slot]));
+    }
+    if (!fused) return;
+
+    // ---- fused RMSNorm epilogue (as in nvfp4_matvec_kernel), among the consumer warps
+    if (lane == 0)
+        for (uint32_t t = 0; t < ta.tokens; ++t) s_sq[warp][t] = sq[t];
+    asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+    if (threadIdx.x < ta.tokens) {
+        float v = 0.f;
+        for (int w = 0; w < kWarps; ++w) v += s_sq[w][threadIdx.x];
+        ep.ws_sumsq[static_cast<uint64_t>(blockIdx.x) * ta.tokens + threadIdx.x] = v;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(ep.ws_count, 1u);
+        s_last = prev == gridDim.x - 1;
+        if (s_last) *ep.ws_count = 0;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+    if (!s_last) return;
+    __threadfence();
+    __shared__ float s_inv[kFusedMaxTokens];
+    if (threadIdx.x < ta.tokens) {
+        float total = 0.f;
+        for (uint32_t c = 0; c < gridDim.x; ++c) total += __ldcg(ep.ws_sumsq + static_cast<uint64_t>(c) * ta.tokens + threadIdx.x);
+        s_inv[threadIdx.x] = rsqrtf(total / static_cast<float>(ta.rows) + ep.eps);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+    float *o = reinterpret_cast<float *>(out);
+    for (uint64_t i = threadIdx.x; i < static_cast<uint64_t>(ta.tokens) * ta.rows; i += kThreads) {
+        const uint32_t t = static_cast<uint32_t>(i / ta.rows), r = static_cast<uint32_t>(i % ta.rows);
+        const float y = __ldcg(o + i) * s_inv[t] * __uint_as_float(static_cast<uint32_t>(ep.weight[r]) << 16);
+        o[i] = y;
+        if (ep.residual_out) ep.residual_out[i] = (ep.residual ? ep.residual[i] : 0.f) + y;
+    }
+}
+
+// rms_norm_f32: one CTA per row; sum of squares in f32 over a strided pass, block reduction, then
+// y = x * rsqrt(mean + eps) * w (shaders/norm.metal:36-81).  Optional residual add into a second
+// output (h = residual + y).
+__global__ void __launch_bounds__(256) rms_norm_kernel(const float *__restrict__ input, const uint16_t *__restrict__ w,
+                                                       float *__restrict__ result, const float *__restrict__ residual,
+                                                       float *__restrict__ residual_out, uint32_t n, float eps) {
+    __shared__ float part[8];
+    const uint64_t base = static_cast<uint64_t>(blockIdx.x) * n;
+    const float *x = input + base;
+    const bool vec = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(input) & 15) == 0);
+    float ss = 0.f;
+    if (vec) {
+        for (uint32_t i = threadIdx.x; i < n / 4; i += blockDim.x) {
+            const float4 v = reinterpret_cast<const float4 *>(x)[i];
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+    } else {
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss += x[i] * x[i];
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (uint32_t k = 0; k < blockDim.x / 32; ++k) tot += part[k];
+    const float inv = rsqrtf(tot / static_cast<float>(n) + eps);
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const float y = x[i] * inv * __uint_as_float(static_cast<uint32_t>(w[i]) << 16);
+        result[base + i] = y;
+        if (residual_out) residual_out[base + i] = (residual ? residual[base + i] : 0.f) + y;
+    }
+}
+
+int check_matvec(const void *input, const uint32_t *codes, const uint8_t *scales, const void *output, uint32_t n,
+                 uint32_t rows, uint32_t tokens, bool in_bf16, const char *name) {
+    if (!input || !codes || !scales || !output) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": null tensor");
+    if (n == 0 || n % 16)
+        return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": hidden_dim must be a positive multiple of 16");
+    if (rows == 0 || tokens == 0) return APEX_OK;
+    if ((reinterpret_cast<uintptr_t>(codes) & 7) || (reinterpret_cast<uintptr_t>(input) & 15))
+        return fail(APEX_ERR_INVALID_ARGUMENT,
+                    std::string(name) + ": codes must be 8-byte and input 16-byte aligned");
+    (void)in_bf16;
+    return APEX_OK;
+}
+
+// The streaming form applies when every tile's codes and scales are whole 16-byte runs at 16-byte
+// offsets (n a multiple of 32, and of 256 unless the rows fill whole tiles) and two stages fit.
+bool stream_plan(const uint32_t *codes, const uint8_t *scales, uint32_t n, uint32_t rows, uint32_t tokens,
+                 TileArgs &ta, uint32_t &grid, size_t &smem) {
+    if (n % 32 || (n % 256 && rows % kTileRows) || (reinterpret_cast<uintptr_t>(codes) & 15) ||
+        (reinterpret_cast<uintptr_t>(scales) & 15))
+        return false;
+    ta.tokens = tokens;
+    ta.rows = rows;
+    ta.n = n;
+    ta.tiles = (rows + kTileRows - 1) / kTileRows;
+    ta.code_bytes = kTileRows * (n / 2);
+    ta.scale_bytes = kTileRows * (n / 16);
+    ta.stage_bytes = (ta.code_bytes + ta.scale_bytes + 127) & ~127u;
+    ta.stages = std::min<uint32_t>(kMaxStages, kStageBudget / ta.stage_bytes);
+    if (ta.stages < 2) return false;
+    ta.stages = std::min<uint32_t>(ta.stages, std::max<uint32_t>(2, ta.tiles));
+    smem = static_cast<size_t>(ta.stages) * ta.stage_bytes;
+    const uint32_t per_sm = smem <= 100u * 1024u ? 2u : 1u;
+    grid = std::min<uint32_t>(ta.tiles, per_sm * static_cast<uint32_t>(sm_count()));
+    ta.status = device_status_ptr();
+    return ta.status != nullptr;
+}
+
+template <typename TIn, typename TOut>
+int launch_matvec(const void *input, const uint32_t *codes, const uint8_t *scales, void *output, uint32_t n,
+                  uint32_t rows, uint32_t tokens, const NormEpilogue &ep, void *stream, const char *name) {
+    TileArgs ta{};
+    uint32_t grid = 0;
+    size_t smem = 0;
+    if (stream_plan(codes, scales, n, rows, tokens, ta, grid, smem)) {
+        auto *kernel = tokens == 1 ? nvfp4_stream_kernel<TIn, TOut, 1> : nvfp4_stream_kernel<TIn, TOut, kTok>;
+        int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(kStageBudget)),
+                            name);
+        if (rc) return rc;
+        kernel<<<grid, kThreads + 32, smem, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const TIn *>(input), codes, scales, static_cast<TOut *>(output), ta, ep);
+        rc = check_cuda(cudaGetLastError(), name);
+        return rc ? rc : ok();
+    }
+    const uint32_t ctas = (rows + kRowsPerCta - 1) / kRowsPerCta;
+    nvfp4_matvec_kernel<TIn, TOut><<<ctas, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const TIn *>(input), codes, scales, static_cast<TOut *>(output), tokens, rows, n, ep);
+    const int rc = check_cuda(cudaGetLastError(), name);
+    return rc ? rc : ok();
+}
+
+}  // namespace
+}  // namespace apex
+
+extern "C" int apex_matmul_nvfp4(const void *input, int input_bf16, const uint32_t *codes, const uint8_t *scales,
+                                 void *output, int output_bf16, uint32_t hidden_dim, uint32_t w_rows,
+                                 uint32_t tokens, void *stream) {
+    using namespace apex;
+    const char *name = "apex_matmul_nvfp4";
+    int rc = check_matvec(input, codes, scales, output, hidden_dim, w_rows, tokens, input_bf16 != 0, name);
+    if (rc) return rc;
+    if (w_rows == 0 || tokens == 0) return ok();
+    const NormEpilogue none{};
+    if (input_bf16)
+        return output_bf16 ? launch_matvec<__nv_bfloat16, __nv_bfloat16>(input, codes, scales, output, hidden_dim, w_rows,
+                                                                           tokens, none, stream, name)
+                           : launch_matvec<__nv_bfloat16, float>(input, codes, scales, output, hidden_dim, w_rows, tokens,
+                                                                  none, stream, name);
+    return output_bf16 ? launch_matvec<float, __nv_bfloat16>(input, codes, scales, output, hidden_dim, w_rows, tokens,
+                                                              none, stream, name)
+                       : launch_matvec<float, float>(input, codes, scales, output, hidden_dim, w_rows, tokens, none,
+                                                     stream, name);
+}
+
+extern "C" int apex_matmul_nvfp4_f32(const float *input, const uint32_t *codes, const uint8_t *scales, float *output,
+                                     uint32_t hidden_dim, uint32_t w_rows, uint32_t tokens, void *stream) {
+    return apex_matmul_nvfp4(input, 0, codes, scales, output, 0, hidden_dim, w_rows, tokens, stream);
+}
+
+extern "C" int apex_rms_norm_f32(const float *input, const uint16_t *weight, float *result, uint32_t rows,
+                                 uint32_t hidden_dim, float eps, void *stream) {
+    using namespace apex;
+    if (rows == 0) return ok();
+    if (!input || !weight || !result) return fail(APEX_ERR_INVALID_ARGUMENT, "apex_rms_norm_f32: null tensor");
+    if (hidden_dim == 0) return fail(APEX_ERR_INVALID_ARGUMENT, "apex_rms_norm_f32: hidden_dim 0");
+    rms_norm_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(input, weight, result, nullptr, nullptr,
+                                                                        hidden_dim, eps);
+    const int rc = check_cuda(cudaGetLastError(), "apex_rms_norm_f32");
+    return rc ? rc : ok();
+}
+
+extern "C" size_t apex_matmul_nvfp4_rms_norm_workspace_bytes(uint32_t w_rows, uint32_t tokens) {
+    // one partial per CTA of whichever form runs (the streaming grid never exceeds the tile count)
+    const size_t ctas = (static_cast<size_t>(w_rows) + apex::kRowsPerCta - 1) / apex::kRowsPerCta;
+    return ((ctas * std::max<uint32_t>(tokens, 1) * sizeof(float) + 255) & ~static_cast<size_t>(255)) + 256;
+}
+
+extern "C" int apex_matmul_nvfp4_rms_norm(const void *input, int input_bf16, const uint32_t *codes,
+                                          const uint8_t *scales, const uint16_t *norm_weight, const float *residual,
+                                          float *output, float *residual_out, uint32_t hidden_dim, uint32_t w_rows,
+                                          uint32_t tokens, float eps, void *workspace, size_t workspace_bytes,
+                                          void *stream) {
+    using namespace apex;
+    const char *name = "apex_matmul_nvfp4_rms_norm";
+    int rc = check_matvec(input, codes, scales, output, hidden_dim, w_rows, tokens, input_bf16 != 0, name);
+    if (rc) return rc;
+    if (w_rows == 0 || tokens == 0) return ok();
+    if (!norm_weight) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": null norm weight");
+    if (tokens > kFusedMaxTokens) {  // prefill-sized: the projection, then the norm as its own launch
+        rc = apex_matmul_nvfp4(input, input_bf16, codes, scales, output, 0, hidden_dim, w_rows, tokens, stream);
+        if (rc) return rc;
+        rms_norm_kernel<<<tokens, 256, 0, static_cast<cudaStream_t>(stream)>>>(output, norm_weight, output, residual,
+                                                                              residual_out, w_rows, eps);
+        rc = check_cuda(cudaGetLastError(), name);
+        return rc ? rc : ok();
+    }
+    const size_t need = apex_matmul_nvfp4_rms_norm_workspace_bytes(w_rows, tokens);
+    if (!workspace || workspace_bytes < need)
+        return fail(APEX_ERR_WORKSPACE, std::string(name) + ": workspace of " + std::to_string(need) + " bytes required");
+    NormEpilogue ep;
+    ep.weight = norm_weight;
+    ep.residual = residual;
+    ep.residual_out = residual_out;
+    ep.ws_sumsq = static_cast<float *>(workspace);
+    ep.ws_count = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(workspace) + need - 256);
+    ep.eps = eps;
+    return input_bf16 ? launch_matvec<__nv_bfloat16, float>(input, codes, scales, output, hidden_dim, w_rows, tokens, ep,
+                                                            stream, name)
+                      : launch_matvec<float, float>(input, codes, scales, output, hidden_dim, w_rows, tokens, ep,
+                                                    stream, name);
+}

@@ -46,6 +46,35 @@ inline void headNormRope(Backend &backend, Buffer *input, Buffer *weights, size_
                 Dim3{tokens, heads}, Dim3{256});
 }
 
+// An NVFP4 matrix [w_rows, hidden_dim] in device memory: codes and scales may live in the same
+// buffer (core.bin) at different offsets (src/ops.h:8-16).
+struct Nvfp4Matrix {
+    Buffer *weights;
+    size_t weights_offset;  // uint32 [w_rows, hidden_dim/8]
+    Buffer *scales;
+    size_t scales_offset;   // uint8 [w_rows, hidden_dim/16]
+    uint32_t w_rows;
+    uint32_t hidden_dim;
+};
+
+// Queue RMSNorm of f32 rows with bf16 weights (src/ops.h:18-27, kernel rms_norm_f32).
+inline void rmsNorm(Backend &backend, Buffer *input, Buffer *weights, size_t weight_offset, Buffer *result,
+                    uint32_t rows, uint32_t hidden_dim, float eps) {
+    backend.run("rms_norm_f32",
+                {Arg::buf(input), Arg::buf(weights, weight_offset), Arg::buf(result), Arg::val(hidden_dim),
+                 Arg::val(eps)},
+                Dim3{rows}, Dim3{256});
+}
+
+// Queue output[t] = W . input[t] for an NVFP4 matrix (src/ops.h:34-46, kernel matmul_nvfp4).
+inline void matmulNvfp4(Backend &backend, Buffer *input, const Nvfp4Matrix &W, Buffer *output, uint32_t tokens) {
+    const uint32_t row_groups = (W.w_rows + 7) / 8;
+    backend.run("matmul_nvfp4",
+                {Arg::buf(input), Arg::buf(W.weights, W.weights_offset), Arg::buf(W.scales, W.scales_offset),
+                 Arg::buf(output), Arg::val(W.hidden_dim), Arg::val(W.w_rows)},
+                Dim3{row_groups, tokens}, Dim3{256});
+}
+
 // Queue the softmax over keys for every (token, q head), scale 1.0, f32 cache
 // (docs/B6_3_attention.md:424-431).
 inline void attention(Backend &backend, Buffer *q, const KvCache &cache, Buffer *output,

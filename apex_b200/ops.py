@@ -289,3 +289,82 @@ def device_status() -> None:
 
 def default_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)
+
+
+# ---------------------------------------------------------------------------- projections and norm
+
+@dataclass
+class Nvfp4Matrix:
+    """The reference's Nvfp4Matrix (src/ops.h:8-16): codes uint32 [w_rows, hidden_dim/8] and E4M3
+    scales uint8 [w_rows, hidden_dim/16], as CUDA tensors (views into one weight buffer work)."""
+    codes: torch.Tensor
+    scales: torch.Tensor
+
+    @property
+    def w_rows(self) -> int:
+        return self.codes.shape[0]
+
+    @property
+    def hidden_dim(self) -> int:
+        return self.codes.shape[1] * 8
+
+
+def _check_matrix(W: Nvfp4Matrix):
+    if W.codes.dtype not in (torch.int32, torch.uint32) or W.scales.dtype != torch.uint8:
+        raise TypeError("Nvfp4Matrix: codes int32/uint32, scales uint8")
+    if W.scales.shape[0] != W.w_rows or W.scales.shape[1] * 16 != W.hidden_dim:
+        raise ValueError("Nvfp4Matrix: scales must be [w_rows, hidden_dim/16]")
+    for t in (W.codes, W.scales):
+        if not t.is_cuda or not t.is_contiguous():
+            raise ValueError("Nvfp4Matrix: CUDA, contiguous tensors")
+
+
+def matmul_nvfp4(input: torch.Tensor, W: Nvfp4Matrix, output: torch.Tensor, tokens: int) -> torch.Tensor:
+    """apex::matmulNvfp4 (src/ops.h:34-46): output[t] = W . input[t].  input [tokens, hidden_dim] f32
+    or bf16; output [tokens, w_rows] f32 or bf16."""
+    _check_matrix(W)
+    if input.dtype not in (torch.float32, torch.bfloat16) or output.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("matmul_nvfp4: input and output float32 or bfloat16")
+    if input.numel() != tokens * W.hidden_dim or output.numel() != tokens * W.w_rows:
+        raise ValueError("matmul_nvfp4: input [tokens, hidden_dim], output [tokens, w_rows]")
+    check(_native.load().apex_matmul_nvfp4(ctypes_ptr(input), int(input.dtype == torch.bfloat16), W.codes.data_ptr(),
+                                           W.scales.data_ptr(), ctypes_ptr(output), int(output.dtype == torch.bfloat16),
+                                           W.hidden_dim, W.w_rows, tokens, _stream()))
+    return output
+
+
+def rms_norm(input: torch.Tensor, weights: torch.Tensor, result: torch.Tensor, rows: int, hidden_dim: int,
+             eps: float) -> torch.Tensor:
+    """apex::rmsNorm (src/ops.h:18-27): f32 rows [rows, hidden_dim], weights bf16 [hidden_dim]."""
+    _need(input, torch.float32, "input")
+    _need(result, torch.float32, "result")
+    if input.numel() != rows * hidden_dim or result.numel() != rows * hidden_dim or weights.numel() != hidden_dim:
+        raise ValueError("rms_norm: shape mismatch")
+    check(_native.load().apex_rms_norm_f32(input.data_ptr(), weights.data_ptr(), result.data_ptr(), rows, hidden_dim,
+                                           eps, _stream()))
+    return result
+
+
+class ProjNormWorkspace:
+    """Device workspace of matmul_nvfp4_rms_norm for up to `tokens` tokens of a w_rows-row matrix."""
+
+    def __init__(self, w_rows: int, tokens: int, device=None):
+        lib = _native.load()
+        self.nbytes = int(lib.apex_matmul_nvfp4_rms_norm_workspace_bytes(w_rows, tokens))
+        self.buffer = torch.zeros(self.nbytes, dtype=torch.uint8, device=device or "cuda")
+
+
+def matmul_nvfp4_rms_norm(input: torch.Tensor, W: Nvfp4Matrix, norm_weight: torch.Tensor, output: torch.Tensor,
+                          tokens: int, eps: float, workspace: ProjNormWorkspace, residual=None,
+                          residual_out=None) -> torch.Tensor:
+    """o_proj followed by the post-attention RMSNorm, fused (apex_matmul_nvfp4_rms_norm): output[t] =
+    rmsnorm(W . input[t], norm_weight); residual_out[t] = residual[t] + output[t] when given."""
+    _check_matrix(W)
+    _need(output, torch.float32, "output")
+    if input.numel() != tokens * W.hidden_dim or output.numel() != tokens * W.w_rows:
+        raise ValueError("matmul_nvfp4_rms_norm: input [tokens, hidden_dim], output [tokens, w_rows]")
+    check(_native.load().apex_matmul_nvfp4_rms_norm(
+        ctypes_ptr(input), int(input.dtype == torch.bfloat16), W.codes.data_ptr(), W.scales.data_ptr(),
+        norm_weight.data_ptr(), _ptr(residual), ctypes_ptr(output), _ptr(residual_out), W.hidden_dim, W.w_rows, tokens,
+        eps, workspace.buffer.data_ptr(), workspace.nbytes, _stream()))
+    return output

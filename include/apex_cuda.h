@@ -270,6 +270,41 @@ APEX_API int apex_attn_prefill_bf16(const apex_attn_params *p, const uint16_t *q
                            uint32_t batch, uint32_t tokens, uint32_t pos0, uint16_t *out,
                            void *workspace, size_t workspace_bytes, void *stream);
 
+/* ------------------------------------------------------------------ projections and norm
+ * The calls either side of the attention path in the reference's attention block
+ * (docs/B6_3_attention.md:15-28): q/k/v projections before it, o projection and the
+ * post-attention RMSNorm after it.  NVFP4 matrix W [w_rows][hidden_dim]: codes uint32
+ * [w_rows][hidden_dim/8] (8 E2M1 codes per word, low nibble first, sign in bit 3) and E4M3 scales
+ * uint8 [w_rows][hidden_dim/16] (src/nvfp4.h:11-43).  hidden_dim a multiple of 16; codes 8-byte
+ * and input 16-byte aligned. */
+
+/* matmul_nvfp4 (shaders/matmul.metal:4-53, launched by apex::matmulNvfp4, src/ops.h:34-46), buffers
+ * in the reference's order: output[t][r] = W[r] . input[t], input [tokens][hidden_dim] f32,
+ * output [tokens][w_rows] f32. */
+APEX_API int apex_matmul_nvfp4_f32(const float *input, const uint32_t *codes, const uint8_t *scales, float *output,
+                                   uint32_t hidden_dim, uint32_t w_rows, uint32_t tokens, void *stream);
+/* The same with bf16 input and / or bf16 output (raw bits) for the bf16 attention path: e.g. the raw
+ * q/k/v rows apex_attn_decode_bf16 takes, or o_proj over its bf16 output. */
+APEX_API int apex_matmul_nvfp4(const void *input, int input_bf16, const uint32_t *codes, const uint8_t *scales,
+                               void *output, int output_bf16, uint32_t hidden_dim, uint32_t w_rows, uint32_t tokens,
+                               void *stream);
+/* rms_norm_f32 (shaders/norm.metal:36-81, apex::rmsNorm, src/ops.h:18-27): result[r] =
+ * input[r] * rsqrt(mean(input[r]^2) + eps) * weight, rows of hidden_dim f32, weight bf16 bits. */
+APEX_API int apex_rms_norm_f32(const float *input, const uint16_t *weight, float *result, uint32_t rows,
+                               uint32_t hidden_dim, float eps, void *stream);
+/* Workspace bytes of apex_matmul_nvfp4_rms_norm (zeroed once before first use, e.g. with
+ * apex_attn_decode_workspace_init; every call leaves it ready for the next). */
+APEX_API size_t apex_matmul_nvfp4_rms_norm_workspace_bytes(uint32_t w_rows, uint32_t tokens);
+/* o_proj with the post-attention RMSNorm fused into its epilogue: output[t] = rmsnorm(W . input[t],
+ * norm_weight) (attn_out of docs/B6_3_attention.md:27-28), and when residual_out is given also
+ * residual_out[t] = residual[t] + output[t] (residual may be NULL: zero).  output [tokens][w_rows]
+ * f32.  Up to 16 tokens it is one launch (the last CTA normalises); more tokens run the norm as a
+ * second launch. */
+APEX_API int apex_matmul_nvfp4_rms_norm(const void *input, int input_bf16, const uint32_t *codes, const uint8_t *scales,
+                                        const uint16_t *norm_weight, const float *residual, float *output,
+                                        float *residual_out, uint32_t hidden_dim, uint32_t w_rows, uint32_t tokens,
+                                        float eps, void *workspace, size_t workspace_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

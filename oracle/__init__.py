@@ -27,6 +27,8 @@ from . import build as _build
 _F32P = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _U16P = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
 _I32P = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_U32P = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+_U8P = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
 _u32, _f32, _i, _sz, _u64 = ctypes.c_uint32, ctypes.c_float, ctypes.c_int, ctypes.c_size_t, ctypes.c_uint64
 
 _lib = None
@@ -68,6 +70,13 @@ def lib():
                                  _F32P, _F32P, _u32, _I32P] + [_u32] * 4 + [_F32P, _i])
         L.orc_partial_row.argtypes = [_F32P, _F32P, _F32P, _sz, _sz, _sz, ctypes.c_double, _F32P]
         L.orc_merge_partials.argtypes = [_F32P, _u32, _sz, _F32P]
+        L.orc_matvec_nvfp4.argtypes = [_U32P, _U8P, _F32P, _F32P, _sz, _sz, _sz]
+        L.orc_rms_norm_rows.argtypes = [_F32P, _U16P_N, _F32P, _sz, _sz, _f32]
+        L.orc_fill_u32.argtypes = [_U32P, _sz, _u64, _u64]
+        L.orc_e2m1.argtypes = [_u32]
+        L.orc_e2m1.restype = _f32
+        L.orc_e4m3.argtypes = [ctypes.c_uint8]
+        L.orc_e4m3.restype = _f32
         L.orc_set_threads.argtypes = [_i]
         L.orc_max_threads.restype = _i
         _lib = L
@@ -88,6 +97,8 @@ def ref_lib():
         R.ref_diff.argtypes = [_F32P, _F32P, _sz, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
         R.ref_head_norm_rope_f32.argtypes = [_F32P, _U16P_N, _F32P] + [_u32] * 5 + [_f32] + [_u32] * 3 + [_f32]
         R.ref_attention.argtypes = [_F32P] * 4 + [_u32] * 7 + [_f32, _I32P_N, _u32]
+        R.ref_matvec_nvfp4.argtypes = [_U32P, _U8P, _F32P, _F32P, _sz, _sz, _sz]
+        R.ref_rms_norm_rows.argtypes = [_F32P, _U16P_N, _F32P, _sz, _sz, _f32]
         _ref = R
     return _ref
 
@@ -224,3 +235,35 @@ def diff(a, b):
     den = float(np.dot(b, b))
     num = float(np.dot(e, e))
     return float(np.abs(e).max(initial=0.0)), math.sqrt(num / den) if den > 0 else math.sqrt(num)
+
+
+# ------------------------------------------------------------------ NVFP4 projections, RMSNorm rows
+
+def fill_u32(n: int, seed: int, stream: int) -> np.ndarray:
+    out = np.empty(int(n), dtype=np.uint32)
+    lib().orc_fill_u32(out, out.size, seed, stream)
+    return out
+
+
+def nvfp4_matrix(rows: int, n: int, seed: int, scale_lo: int = 0x20, scale_hi: int = 0x40):
+    """Synthetic NVFP4 matrix [rows][n]: uniform codes and E4M3 scales in [scale_lo, scale_hi]
+    (positive, finite; 0x20..0x40 is 2^-3 .. 2)."""
+    codes = fill_u32(rows * n // 8, seed, 7).reshape(rows, n // 8)
+    scales = uniform_int(rows * n // 16, seed, 8, scale_lo, scale_hi).astype(np.uint8).reshape(rows, n // 16)
+    return codes, scales
+
+
+def matvec_nvfp4(codes, scales, inp, tokens, rows, n, *, ref=False):
+    out = np.zeros(tokens * rows, np.float32)
+    L = ref_lib() if ref else lib()
+    fn = L.ref_matvec_nvfp4 if ref else L.orc_matvec_nvfp4
+    fn(_c(codes, np.uint32).ravel(), _c(scales, np.uint8).ravel(), _c(inp).ravel(), out, tokens, rows, n)
+    return out.reshape(tokens, rows)
+
+
+def rms_norm_rows(inp, w, rows, n, eps, *, ref=False):
+    out = np.zeros(rows * n, np.float32)
+    L = ref_lib() if ref else lib()
+    fn = L.ref_rms_norm_rows if ref else L.orc_rms_norm_rows
+    fn(_c(inp).ravel(), None if w is None else _c(w, np.uint16), out, rows, n, eps)
+    return out.reshape(rows, n)

@@ -18,6 +18,13 @@
  *   - orc_attention_f32   docs/B6_3_attention.md:282-344 (GQA map h/(Hq/Hkv), window rule
  *                         first = window && pos+1 > window ? pos+1-window : 0) and the CPU
  *                         loop of docs/B6_3_attention.md:661-670
+ *   - orc_e2m1 / orc_e4m3  src/nvfp4.h:11-28 (E2M1 table with sign in bit 3; finite E4M3,
+ *                         exponent bias 7, e == 0 subnormal m/512)
+ *   - orc_matvec_nvfp4    src/tests/cpu_ref.h:48-63 with src/nvfp4.h:31-43: every weight row
+ *                         decoded (code i of a 16-weight group at word 2g + i/8, nibble i%8, times
+ *                         the group's E4M3 scale), then dotted with each token in double
+ *   - orc_rms_norm_rows   shaders/norm.metal:36-81 on rows of a [rows][n] matrix with the
+ *                         arithmetic of orc_rms_norm (cpu_ref.h:14-25)
  * plus compositions for the bf16 configurations (prefill with K/V cache append, ragged
  * decode, split-KV partials and their log-sum-exp merge), a bf16 rounding helper and the
  * seeded synthetic-input generator shared by the tests and the golden fixtures.
@@ -369,4 +376,59 @@ void orc_merge_partials(const float *parts, uint32_t R, size_t D, float *out) {
         }
         out[d] = (float)(num / den);
     }
+}
+
+/* ---------------------------------------------------------------- NVFP4 projections */
+
+/* src/nvfp4.h:11-16 */
+float orc_e2m1(uint32_t code) {
+    static const float table[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    const float v = table[code & 7u];
+    return (code & 8u) ? -v : v;
+}
+
+/* src/nvfp4.h:18-28 */
+float orc_e4m3(uint8_t byte) {
+    const uint32_t e = (byte >> 3) & 0xFu, m = byte & 7u;
+    const float v = e == 0 ? (float)m * (1.0f / 512.0f) : ldexpf(1.0f + (float)m * 0.125f, (int)e - 7);
+    return (byte & 0x80u) ? -v : v;
+}
+
+/* output[t * rows + r] = W[r] . input[t] for W [rows][n] in NVFP4: codes uint32 [rows][n/8]
+ * (8 codes per word, low nibble first), scales E4M3 [rows][n/16].  src/tests/cpu_ref.h:48-63. */
+void orc_matvec_nvfp4(const uint32_t *codes, const uint8_t *scales, const float *input, float *output,
+                      size_t tokens, size_t rows, size_t n) {
+#pragma omp parallel
+    {
+        float *w = (float *)malloc(n * sizeof(float));
+#pragma omp for schedule(static)
+        for (long long r = 0; r < (long long)rows; ++r) {
+            const uint32_t *cr = codes + (size_t)r * (n / 8);
+            const uint8_t *sr = scales + (size_t)r * (n / 16);
+            for (size_t g = 0; g < n / 16; ++g) {
+                const float sc = orc_e4m3(sr[g]);
+                for (size_t i = 0; i < 16; ++i) {
+                    const uint32_t word = cr[2 * g + i / 8];
+                    w[g * 16 + i] = orc_e2m1((word >> (4 * (i % 8))) & 0xFu) * sc;
+                }
+            }
+            for (size_t t = 0; t < tokens; ++t) {
+                double acc = 0.0;
+                for (size_t i = 0; i < n; ++i) acc += (double)w[i] * input[t * n + i];
+                output[t * rows + (size_t)r] = (float)acc;
+            }
+        }
+        free(w);
+    }
+}
+
+/* shaders/norm.metal:36-81 (one row per threadgroup) with cpu_ref.h:14-25 arithmetic. */
+void orc_rms_norm_rows(const float *input, const uint16_t *w, float *output, size_t rows, size_t n, float eps) {
+    for (size_t r = 0; r < rows; ++r) orc_rms_norm(input + r * n, w, output + r * n, n, eps);
+}
+
+/* Raw 32-bit words of the seeded generator (codes of synthetic NVFP4 matrices). */
+void orc_fill_u32(uint32_t *out, size_t n, uint64_t seed, uint64_t stream) {
+    const uint64_t key = rng_key(seed, stream);
+    for (size_t i = 0; i < n; ++i) out[i] = (uint32_t)(rng_bits(key, i) >> 16);
 }

@@ -46,6 +46,18 @@ void ref_attention_row(const float* q, const float* K, const float* V, float* ou
     attentionRowCpu(q, K, V, out, head_dim, first, last);
 }
 
+// matvecNvfp4Cpu (src/tests/cpu_ref.h:48-63): output[t, :] = W . input[t, :], NVFP4 W [rows][n].
+void ref_matvec_nvfp4(const uint32_t* codes, const uint8_t* scales, const float* input, float* output,
+                      size_t tokens, size_t rows, size_t n) {
+    matvecNvfp4Cpu(codes, scales, input, output, tokens, rows, n);
+}
+
+// rms_norm_f32 semantics (shaders/norm.metal:36-81) through rmsNormCpu, one row at a time, as the
+// reference's test-norm computes its CPU answer (src/tests/test_norm.cpp:74-79).
+void ref_rms_norm_rows(const float* input, const uint16_t* w, float* output, size_t rows, size_t n, float eps) {
+    for (size_t r = 0; r < rows; ++r) rmsNormCpu(input + r * n, w ? w : ones_bf16(n), output + r * n, n, eps);
+}
+
 void ref_diff(const float* a, const float* b, size_t n, double* max_abs, double* rel_l2) {
     const Diff d = diff(a, b, n);
     *max_abs = d.max_abs;

@@ -27,6 +27,8 @@ void orc_kv_append(const float *, const uint16_t *, int, uint32_t, float, float,
 void orc_prefill(const float *, const float *, const float *, const uint16_t *, const uint16_t *, int, int,
                  uint32_t, float, float, float, uint32_t, float *, float *, uint32_t, uint32_t, uint32_t, uint32_t,
                  uint32_t, uint32_t, const int32_t *, uint32_t, float *, int);
+void orc_matvec_nvfp4(const uint32_t *, const uint8_t *, const float *, float *, size_t, size_t, size_t);
+void orc_rms_norm_rows(const float *, const uint16_t *, float *, size_t, size_t, float);
 }
 
 namespace {
@@ -194,6 +196,42 @@ void test_bf16_prefill_decode(apex::CudaBackend &be) {
     for (auto *b : {qb, kb, vb, qwb, kwb, cache.k, cache.v, o, ws, qdb, kdb, vdb, lens, od, wsd}) be.release(b);
 }
 
+// The reference's test-norm / test-mlp call pattern (src/tests/test_norm.cpp:67-71,
+// src/tests/dense_mlp.cpp:92-96): rmsNorm, then matmulNvfp4 with codes and scales at offsets in one
+// weight buffer, queued through the Backend and compared after sync() with the reference gate.
+void test_norm_and_nvfp4(apex::CudaBackend &be) {
+    const uint32_t T = 3, H = 2816, R = 200;
+    auto x = normal(size_t(T) * H, 31, 2.f);
+    auto nw = weights(H, 32);
+    std::mt19937 rng(33);
+    std::vector<uint32_t> codes(size_t(R) * H / 8);
+    for (auto &c : codes) c = rng();
+    std::vector<uint8_t> scales(size_t(R) * H / 16);
+    for (auto &sc : scales) sc = uint8_t(0x20 + rng() % 0x20);
+    // one weight buffer: norm weight, then codes, then scales (offsets as core.bin would give them)
+    const size_t off_codes = 16384, off_scales = off_codes + codes.size() * 4;
+    std::vector<uint8_t> blob(off_scales + scales.size(), 0);
+    std::memcpy(blob.data(), nw.data(), nw.size() * 2);
+    std::memcpy(blob.data() + off_codes, codes.data(), codes.size() * 4);
+    std::memcpy(blob.data() + off_scales, scales.data(), scales.size());
+    apex::Buffer *wb = upload(be, blob.data(), blob.size(), "weights");
+    apex::Buffer *in = upload(be, x.data(), x.size() * 4, "activations");
+    apex::Buffer *normed = be.allocate(x.size() * 4, "activations");
+    apex::Buffer *out = be.allocate(size_t(T) * R * 4, "activations");
+    apex::rmsNorm(be, in, wb, 0, normed, T, H, 1e-6f);
+    const apex::Nvfp4Matrix W{wb, off_codes, wb, off_scales, R, H};
+    apex::matmulNvfp4(be, normed, W, out, T);
+    be.sync();
+    std::vector<float> nref(x.size()), oref(size_t(T) * R);
+    orc_rms_norm_rows(x.data(), nw.data(), nref.data(), T, H, 1e-6f);
+    orc_matvec_nvfp4(codes.data(), scales.data(), nref.data(), oref.data(), T, R, H);
+    Diff d = diff(static_cast<float *>(be.contents(normed)), nref.data(), nref.size());
+    report("rmsNorm (f32, hidden 2816)", d, d.rel_l2 < 1e-5);
+    d = diff(static_cast<float *>(be.contents(out)), oref.data(), oref.size());
+    report("matmulNvfp4 (f32 in/out, offsets in one buffer)", d, d.rel_l2 < 1e-5);
+    for (auto *b : {wb, in, normed, out}) be.release(b);
+}
+
 }  // namespace
 
 int main() {
@@ -204,6 +242,7 @@ int main() {
         test_attention_block(backend, false);
         test_attention_block(backend, true);
         test_bf16_prefill_decode(backend);
+        test_norm_and_nvfp4(backend);
         apex::PhaseTable::get().print(stdout);
         apex::MemoryLedger::get().print(stdout);
     } catch (const std::exception &e) {

@@ -8,7 +8,12 @@ oracle/apex_oracle.c (index scheme in apex_b200/configs.py), so only outputs, ar
 input checksums are stored.  Everything is f32 (the fp32 reference the tolerance is stated
 against); files are ``<f4`` .npy, the format src/npy.h reads.
 
-Usage (needs the reference tree to build oracle/_ref):  python tests/golden/make_goldens.py
+The NVFP4 projection and RMSNorm cases come from the reference's matvecNvfp4Cpu
+(src/tests/cpu_ref.h:48-63, with src/nvfp4.h) and rmsNormCpu on seeded synthetic matrices.
+
+Usage (needs the reference tree to build oracle/_ref):
+    python tests/golden/make_goldens.py            # every case
+    python tests/golden/make_goldens.py --only nvfp4_matvec,rms_norm_rows,oproj_post_norm
 """
 from __future__ import annotations
 
@@ -81,19 +86,64 @@ def ref_rows(cfg, b, positions, L):
     return np.stack(out).reshape(len(positions), cfg.q_heads, cfg.head_dim), kv_digest
 
 
+PROJ_CASES = {
+    # (w_rows, hidden_dim, tokens, seed): a small matrix, and o_proj of a sliding layer (2816 x 4096)
+    "nvfp4_matvec": dict(rows=48, n=256, tokens=3, seed=300),
+    "rms_norm_rows": dict(rows=3, n=2816, seed=301),
+    "oproj_post_norm": dict(rows=2816, n=4096, tokens=2, seed=302),
+}
+
+
+def proj_inputs(name):
+    """Seeded inputs of a projection / norm case (also used by the tests)."""
+    c = PROJ_CASES[name]
+    if name == "rms_norm_rows":
+        x = oracle.bf16_to_f32(oracle.normal_bf16(c["rows"] * c["n"], c["seed"], 1)).reshape(c["rows"], c["n"]) * 3.0
+        w = oracle.normal_bf16(c["n"], c["seed"], 4, 0, 1.0, 0.1)
+        return x, w
+    codes, scales = oracle.nvfp4_matrix(c["rows"], c["n"], c["seed"])
+    x = oracle.bf16_to_f32(oracle.normal_bf16(c["tokens"] * c["n"], c["seed"], 1)).reshape(c["tokens"], c["n"])
+    w = oracle.normal_bf16(c["rows"], c["seed"], 4, 0, 1.0, 0.1)
+    return codes, scales, x, w
+
+
+def proj_goldens(save):
+    for name, c in PROJ_CASES.items():
+        if name == "rms_norm_rows":
+            x, w = proj_inputs(name)
+            out = oracle.rms_norm_rows(x, w, c["rows"], c["n"], 1e-6, ref=True)
+            save(name, out, dict(c, eps=1e-6, input_sha=sha(x, w)))
+            continue
+        codes, scales, x, w = proj_inputs(name)
+        out = oracle.matvec_nvfp4(codes, scales, x, c["tokens"], c["rows"], c["n"], ref=True)
+        if name == "oproj_post_norm":
+            out = oracle.rms_norm_rows(out, w, c["tokens"], c["rows"], 1e-6, ref=True)
+        save(name, out, dict(c, eps=1e-6, input_sha=sha(codes, scales, x, w)))
+
+
 def main() -> int:
     if oracle.ref_lib() is None:
         print("reference tree not available: cannot build oracle/_ref", file=sys.stderr)
         return 1
+    only = None
+    if len(sys.argv) > 2 and sys.argv[1] == "--only":
+        only = set(sys.argv[2].split(","))
     manifest = {"generator": "oracle/apex_oracle.c orc_fill_normal_bf16 (splitmix64 + Box-Muller)",
                 "source": "oracle/_ref (reference cpu_ref.h + docs/B6_3_attention.md section 5)",
                 "cases": {}}
+    if only is not None:
+        manifest = json.loads((OUT / "manifest.json").read_text())
     R = oracle.ref_lib()
 
     def save(name, arr, meta):
         np.save(OUT / f"{name}.npy", np.ascontiguousarray(arr, dtype="<f4"))
         manifest["cases"][name] = meta
         print(name, arr.shape)
+
+    if only is not None:
+        proj_goldens(lambda name, arr, meta: save(name, arr, meta) if name in only else None)
+        (OUT / "manifest.json").write_text(json.dumps(manifest, indent=1) + "\n")
+        return 0
 
     # 1. head_norm_rope_f32 -- the shipped kernel's semantics (shaders/head_norm_rope.metal).
     hnr = [
@@ -172,6 +222,7 @@ def main() -> int:
     save("c5_long_decode_b8_seq7", out,
          dict(config=c5b.name, seq=7, positions=[L - 1], context=L, kv_sha=d))
 
+    proj_goldens(save)
     (OUT / "manifest.json").write_text(json.dumps(manifest, indent=1) + "\n")
     return 0
 

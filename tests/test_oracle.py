@@ -4,6 +4,7 @@ cross-checked against that code live (when oracle/_ref is built), and against cl
 from __future__ import annotations
 
 import hashlib
+import pathlib
 
 import numpy as np
 import pytest
@@ -182,3 +183,33 @@ def test_generator_is_sliceable_and_standard_normal():
     np.testing.assert_array_equal(a, b)
     x = oracle.bf16_to_f32(oracle.normal_bf16(1 << 20, 9, 1))
     assert abs(float(x.mean())) < 5e-3 and abs(float(x.std()) - 1.0) < 5e-3
+
+
+def test_nvfp4_and_rms_norm_restatement_equals_reference_goldens():
+    """The C restatement of matvecNvfp4Cpu / rmsNormCpu reproduces the goldens made by the
+    reference's own code bit for bit, on the recorded inputs."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("make_goldens", pathlib.Path(__file__).parent / "golden" / "make_goldens.py")
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    man = manifest()
+    for name, c in mg.PROJ_CASES.items():
+        if name == "rms_norm_rows":
+            x, w = mg.proj_inputs(name)
+            assert mg.sha(x, w) == man[name]["input_sha"]
+            got = oracle.rms_norm_rows(x, w, c["rows"], c["n"], 1e-6)
+        else:
+            codes, scales, x, w = mg.proj_inputs(name)
+            assert mg.sha(codes, scales, x, w) == man[name]["input_sha"]
+            got = oracle.matvec_nvfp4(codes, scales, x, c["tokens"], c["rows"], c["n"])
+            if name == "oproj_post_norm":
+                got = oracle.rms_norm_rows(got, w, c["tokens"], c["rows"], 1e-6)
+        np.testing.assert_array_equal(got, golden(name))
+
+
+def test_e2m1_e4m3_tables():
+    L = oracle.lib()
+    assert [L.orc_e2m1(c) for c in range(8)] == [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+    assert [L.orc_e2m1(c | 8) for c in range(1, 8)] == [-0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
+    assert L.orc_e4m3(0x38) == 1.0 and L.orc_e4m3(0x01) == 2.0 ** -9 and L.orc_e4m3(0x7E) == 448.0
+    assert L.orc_e4m3(0xB8) == -1.0
