@@ -35,6 +35,7 @@ class AttnConfig:
     eps: float = 1e-6
     qk_norm: bool = True
     v_norm: bool = False
+    partial_rope: int = 0         # pairs rotated when not all of them (the global layers' 64 of 256)
     note: str = field(default="", compare=False)
 
     @property
@@ -43,7 +44,7 @@ class AttnConfig:
 
     @property
     def rope_pairs(self) -> int:
-        return self.head_dim // 2
+        return self.partial_rope or self.head_dim // 2
 
 
 CONFIGS = {
@@ -65,6 +66,16 @@ CONFIGS = {
     "c5_long_decode_b8": AttnConfig(
         "c5_long_decode_b8", "decode", batch=8, seed=4, rope_theta=1e6, context=131072,
         note="eight 131072-key decodes; KV split across GPUs"),
+    # the reference model's global ("full attention") layers: 16 q / 2 kv heads of head_dim 512, RoPE on
+    # the first 64 of 256 pairs, theta 1e6, weightless RMSNorm of V (docs/B6_3_attention.md:46-60)
+    "global_decode": AttnConfig(
+        "global_decode", "decode", batch=8, seed=11, rope_theta=1e6, context=32768, q_heads=16, kv_heads=2,
+        head_dim=512, v_norm=True, partial_rope=64,
+        note="global-layer decode: 8 x 32768 keys, 2 kv heads of 512, GQA group 8"),
+    # not an attention configuration: the NVFP4 projections either side of one decode step
+    "proj_decode": AttnConfig(
+        "proj_decode", "proj", batch=1, seed=9, rope_theta=1e4,
+        note="q/k/v and o_proj + post-attention norm of one decode token, sliding-layer shapes"),
 }
 
 

@@ -1042,6 +1042,7 @@ int launch_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16
 extern "C" size_t apex_attn_decode_workspace_bytes(const apex_attn_params *p, uint32_t batch,
                                                    uint32_t max_seq_len) {
     if (!p || p->kv_heads == 0) return 0;
+    if (apex::gqa_decode_form(p)) return apex::gqa_workspace_bytes(p, batch, std::max<uint32_t>(max_seq_len, 1));
     return apex::workspace_bytes(batch, p->q_heads, p->kv_heads, std::max<uint32_t>(max_seq_len, 1));
 }
 
@@ -1061,6 +1062,10 @@ extern "C" int apex_attn_decode_bf16(const apex_attn_params *p, const uint16_t *
                                      const int32_t *seq_lens, uint32_t batch,
                                      uint32_t max_seq_len, uint16_t *out, void *workspace,
                                      size_t workspace_bytes, void *stream) {
+    if (apex::gqa_decode_form(p))
+        return apex::launch_gqa_decode(p, q_raw, k_new, v_new, q_norm_w, k_norm_w, k_cache, v_cache, capacity,
+                                       seq_lens, batch, max_seq_len, out, workspace, workspace_bytes, stream,
+                                       "apex_attn_decode_bf16");
     return apex::launch_decode(p, q_raw, k_new, v_new, q_norm_w, k_norm_w, k_cache, v_cache,
                                capacity, seq_lens, batch, max_seq_len, 0, 0xffffffffu, false, out,
                                nullptr, workspace, workspace_bytes, stream, "apex_attn_decode_bf16");

@@ -40,4 +40,13 @@ void rope_table(float *inv_freq, uint32_t pairs, uint32_t head_dim, float base);
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Decode for wide GQA groups / head_dim 512 (decode_gqa.cu): whether `p` takes that form, its
+// workspace size, and the launch (same arguments as apex_attn_decode_bf16).
+bool gqa_decode_form(const apex_attn_params *p);
+size_t gqa_workspace_bytes(const apex_attn_params *p, uint32_t batch, uint32_t max_len);
+int launch_gqa_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t *k_new, const uint16_t *v_new,
+                      const uint16_t *q_w, const uint16_t *k_w, uint16_t *k_cache, uint16_t *v_cache,
+                      uint32_t capacity, const int32_t *seq_lens, uint32_t batch, uint32_t max_seq_len,
+                      uint16_t *out, void *workspace, size_t workspace_bytes_given, void *stream, const char *name);
+
 }  // namespace apex

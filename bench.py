@@ -53,7 +53,8 @@ sys.path.insert(0, str(ROOT))
 from apex_b200.configs import CONFIGS, decode_bytes, prefill_flops, visible_pairs  # noqa: E402
 
 PRIMARY = "c5_long_decode_b8"
-ALSO = ("c1_decode", "c2_prefill_window", "c3_ragged_decode", "c4_chunked_prefill", "c5_long_decode_b1")
+ALSO = ("c1_decode", "c2_prefill_window", "c3_ragged_decode", "c4_chunked_prefill", "c5_long_decode_b1",
+        "proj_decode")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_BYTES = 126 * 1024 * 1024
 TOL_MAX, TOL_MEAN = 2e-2, 2e-3          # against an fp32 reference
@@ -481,6 +482,103 @@ class DecodeWorkload:
             self.peer = None
 
 
+class ProjWorkload:
+    """The projections either side of one decode step of a sliding layer of the reference model
+    (docs/B6_3_attention.md:46-60): q (4096 x 2816), k and v (2048 x 2816) from the f32 normed
+    hidden state to bf16 raw rows (what the fused decode takes), and o_proj (2816 x 4096) over the
+    bf16 attention output with the post-attention RMSNorm fused in its epilogue.  NVFP4 weights
+    (E2M1 codes, E4M3 per-16 scales); one step = the four calls; algorithmic bytes = weight codes +
+    scales + activations.  N > 1: replicas."""
+    kind = "proj"
+    SHAPES = (("q", 4096, 2816), ("k", 2048, 2816), ("v", 2048, 2816), ("o", 2816, 4096))
+
+    def __init__(self, cfg, device, rank=0, world=1):
+        import torch
+        from apex_b200 import ops
+        self.ops, self.torch, self.cfg = ops, torch, cfg
+        self.sharding = "replica"
+        g = torch.Generator(device=device).manual_seed(900 + rank)
+        wbytes = sum(r * n // 2 + r * n // 16 for _, r, n in self.SHAPES)
+        self.R = max(2, math.ceil(2 * L2_BYTES / wbytes) + 1)
+
+        def matrix(r, n):
+            codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (r, n // 8), generator=g, dtype=torch.int32, device=device)
+            scales = torch.randint(0x20, 0x40, (r, n // 16), generator=g, dtype=torch.uint8, device=device)
+            return ops.Nvfp4Matrix(codes, scales)
+
+        self.sets = [{k: matrix(r, n) for k, r, n in self.SHAPES} for _ in range(self.R)]
+        self.x = torch.randn(1, 2816, generator=g, device=device)
+        self.att = torch.randn(1, 4096, generator=g, device=device).to(torch.bfloat16)
+        self.nw = (torch.randn(2816, generator=g, device=device) * 0.1 + 1.0).to(torch.bfloat16)
+        self.q = torch.empty(1, 4096, dtype=torch.bfloat16, device=device)
+        self.k = torch.empty(1, 2048, dtype=torch.bfloat16, device=device)
+        self.v = torch.empty(1, 2048, dtype=torch.bfloat16, device=device)
+        self.o = torch.empty(1, 2816, device=device)
+        self.ws = ops.ProjNormWorkspace(2816, 1, device=device)
+        self.bytes = wbytes + 2816 * 4 + 4096 * 2 + (4096 + 2048 * 2) * 2 + 2816 * 4
+        self.units = self.bytes
+        self.tokens = 1
+        self.launches_per_step = 4
+        self.kernel_name = "nvfp4_stream_kernel (q, k, v, fused o_proj + rms_norm)"
+
+    def _run(self, W, x, att, q, k, v, o):
+        ops = self.ops
+        ops.matmul_nvfp4(x, W["q"], q, 1)
+        ops.matmul_nvfp4(x, W["k"], k, 1)
+        ops.matmul_nvfp4(x, W["v"], v, 1)
+        ops.matmul_nvfp4_rms_norm(att, W["o"], self.nw, o, 1, 1e-6, self.ws)
+
+    def step(self, i):
+        self._run(self.sets[i % self.R], self.x, self.att, self.q, self.k, self.v, self.o)
+
+    def dominant_launches(self, i, record):
+        record(lambda: self.step(i))
+        return self.bytes
+
+    def roofline_work(self):
+        return self.bytes, "hbm"
+
+    def e2e_inputs(self):
+        return [self.x, self.att], self.o
+
+    def e2e_compute(self, ins, out):
+        self._run(self.sets[0], ins[0], ins[1], self.q, self.k, self.v, out)
+
+    def parity(self):
+        """Against the weights decoded in torch (E2M1 table x E4M3 scale) and fp64 dot products:
+        rel-L2 < 1e-5 for the f32 output (the reference's gate), bf16 rounding for the bf16 rows."""
+        torch = self.torch
+        self.step(0)
+        torch.cuda.synchronize()
+        self.ops.device_status()
+        W = self.sets[0]
+        lut = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6], dtype=torch.float64,
+                           device=self.x.device)
+
+        def dense(M):
+            c = M.codes.view(torch.int32)
+            nib = torch.stack([(c >> (4 * j)) & 0xF for j in range(8)], -1).reshape(c.shape[0], -1).long()
+            b = M.scales.long()
+            e, m = (b >> 3) & 0xF, (b & 7).double()
+            sc = torch.where(e == 0, m / 512.0, (1 + m / 8) * torch.pow(2.0, (e - 7).double()))
+            sc = torch.where((b & 0x80) != 0, -sc, sc)
+            return lut[nib] * sc.repeat_interleave(16, 1)
+
+        worst, rel = 0.0, 0.0
+        for name, out in (("q", self.q), ("k", self.k), ("v", self.v)):
+            ref = (dense(W[name]) @ self.x.double().T).T
+            err = ((out.double() - ref).abs() / ref.abs().clamp_min(1e-3)).max().item()
+            worst = max(worst, err)
+        ro = (dense(W["o"]) @ self.att.double().T).T
+        ro = ro * torch.rsqrt((ro ** 2).mean(-1, keepdim=True) + 1e-6) * self.nw.double()
+        rel = ((self.o.double() - ro).norm() / ro.norm()).item()
+        return {"max_abs": worst, "mean_abs": rel, "o_proj_norm_rel_l2": rel, "qkv_bf16_max_rel": worst,
+                "ref": "torch fp64: weights decoded from the E2M1 / E4M3 bits", "ok": rel < 1e-5 and worst <= 2 ** -8}
+
+    def close(self):
+        pass
+
+
 # ---------------------------------------------------------------------------- reference arm (CPU)
 
 _REF_CACHE = {}
@@ -519,6 +617,21 @@ def cpu_reference_step(cfg, threads):
     oracle.set_threads(threads)
     ref = oracle.ref_lib() is not None
     kind = "reference" if ref else "port"
+    if cfg.kind == "proj":  # matvecNvfp4Cpu on the four projections of one decode token, then rmsNormCpu
+        key = ("proj",)
+        if key not in _REF_CACHE:
+            _REF_CACHE[key] = [oracle.nvfp4_matrix(r, n, 900 + i) + (r, n)
+                               for i, (_, r, n) in enumerate(ProjWorkload.SHAPES)]
+        mats = _REF_CACHE[key]
+        nw = oracle.normal_bf16(2816, 900, 4, 0, 1.0, 0.1)
+        xs = {n: np.random.default_rng(n).standard_normal((1, n)).astype(np.float32) for _, _, n in ProjWorkload.SHAPES}
+        t0 = time.perf_counter()
+        for codes, scales, r, n in mats:
+            y = oracle.matvec_nvfp4(codes, scales, xs[n], 1, r, n, ref=ref)
+        oracle.rms_norm_rows(y, nw, 1, 2816, 1e-6, ref=ref)
+        dt = time.perf_counter() - t0
+        nbytes = sum(r * n // 2 + r * n // 16 for _, r, n in ProjWorkload.SHAPES)
+        return dt, nbytes, "the four projections of one decode token (matvecNvfp4Cpu) + rmsNormCpu; value = weight bytes / time", kind
     Hq, Hkv, D = cfg.q_heads, cfg.kv_heads, cfg.head_dim
     if cfg.kind == "prefill":
         # c2: the whole prompt; c4: 16 query rows of the last chunk of sequence 0 (the cache of the
@@ -595,6 +708,8 @@ def cpu_reference_step(cfg, threads):
 def metric_of(cfg):
     if cfg.kind == "prefill":
         return "prefill attn TFLOP/s", "TFLOP/s", 1e12
+    if cfg.kind == "proj":
+        return "decode projections GB/s", "GB/s", 1e9
     return "decode attn KV GB/s", "GB/s", 1e9
 
 
@@ -606,6 +721,9 @@ def cpu_baseline(cfg, threads):
 
 
 def config_of(cfg):
+    if cfg.kind == "proj":
+        return {"workload": cfg.name, "tokens": 1, "matrices": {k: [r, n] for k, r, n in ProjWorkload.SHAPES},
+                "weights": "NVFP4 (E2M1 codes, E4M3 per-16 scales)", "fused": "o_proj + post-attention rms_norm"}
     c = {"workload": cfg.name, "batch": cfg.batch, "q_heads": cfg.q_heads, "kv_heads": cfg.kv_heads,
          "head_dim": cfg.head_dim, "window": cfg.window, "rope_theta": cfg.rope_theta,
          "qk_norm": cfg.qk_norm, "scale": "1/sqrt(head_dim)"}
@@ -854,7 +972,7 @@ def measure(wl, cfg, K, W, ctx):
     kern_ms = kern_ms_total / len(spans)
 
     # end to end through the fused C-ABI call, host buffers, copies inside the timed region
-    KE = min(K, 50 if wl.kind == "decode" else 20)
+    KE = min(K, 50 if wl.kind != "prefill" else 20)
     e2e_ms, h2d_bytes, d2h_bytes, e2e_mode = run_e2e(wl, KE, world, dist)
     e2e_t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
     if world > 1:
@@ -915,8 +1033,9 @@ def run_ours(args, names):
     reports = {}
     for j, name in enumerate(names):
         cfg = CONFIGS[name]
-        K = args.steps if j == 0 else min(args.steps, 50 if cfg.kind == "decode" else 20)
-        wl = (PrefillWorkload if cfg.kind == "prefill" else DecodeWorkload)(cfg, device, rank, world)
+        K = args.steps if j == 0 else min(args.steps, 50 if cfg.kind != "prefill" else 20)
+        wl = {"prefill": PrefillWorkload, "decode": DecodeWorkload, "proj": ProjWorkload}[cfg.kind](cfg, device, rank,
+                                                                                                  world)
         try:
             reports[name] = measure(wl, cfg, K, args.warmup, ctx)
         finally:

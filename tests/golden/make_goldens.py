@@ -107,6 +107,29 @@ def proj_inputs(name):
     return codes, scales, x, w
 
 
+def global_goldens(save):
+    """Global-layer decode (head_dim 512, 2 kv heads, RoPE on 64 pairs, V normalised): the cache of
+    sequence b built by the reference's head_norm_rope (K: weight + partial RoPE; V: weightless norm)
+    and its attention row at the last position."""
+    cfg = CONFIGS["global_decode"]
+    R = oracle.ref_lib()
+    Hq, Hkv, D = cfg.q_heads, cfg.kv_heads, cfg.head_dim
+    qw, kw = I.norm_weights(cfg)
+    outs, meta = [], []
+    for b, L in ((0, 3000), (5, 17)):
+        k = oracle.bf16_to_f32(I.k_rows(cfg, b, 0, L)).ravel()
+        v = oracle.bf16_to_f32(I.v_rows(cfg, b, 0, L)).ravel()
+        Kc = np.zeros(Hkv * L * D, np.float32)
+        Vc = np.zeros(Hkv * L * D, np.float32)
+        R.ref_head_norm_rope_f32(k, kw, Kc, L, Hkv, D, 1, cfg.rope_pairs, cfg.rope_theta, 0, D, L * D, cfg.eps)
+        R.ref_head_norm_rope_f32(v, None, Vc, L, Hkv, D, 0, 0, cfg.rope_theta, 0, D, L * D, cfg.eps)
+        qn = ref_query(cfg, b, L - 1, qw)
+        out = oracle.attention_f32(qn, Kc, Vc, 1, Hq, Hkv, D, L, L - 1, cfg.window, cfg.scale, ref=True)
+        outs.append(out.reshape(Hq, D))
+        meta.append(dict(seq=b, context=L, kv_sha=sha(k, v)))
+    save("global_decode", np.stack(outs), dict(config=cfg.name, rows=meta))
+
+
 def proj_goldens(save):
     for name, c in PROJ_CASES.items():
         if name == "rms_norm_rows":
@@ -142,6 +165,7 @@ def main() -> int:
 
     if only is not None:
         proj_goldens(lambda name, arr, meta: save(name, arr, meta) if name in only else None)
+        global_goldens(lambda name, arr, meta: save(name, arr, meta) if name in only else None)
         (OUT / "manifest.json").write_text(json.dumps(manifest, indent=1) + "\n")
         return 0
 
@@ -223,6 +247,7 @@ def main() -> int:
          dict(config=c5b.name, seq=7, positions=[L - 1], context=L, kv_sha=d))
 
     proj_goldens(save)
+    global_goldens(save)
     (OUT / "manifest.json").write_text(json.dumps(manifest, indent=1) + "\n")
     return 0
 

@@ -65,10 +65,18 @@ def fill_k_cache(cache_k_b, k_rows_u16, w_u16, cfg, pos0=0):
                        cfg.rope_pairs, cfg.rope_theta, pos0, D, cap * D, cfg.eps)
 
 
-def fill_v_cache(cache_v_b, v_rows_u16, pos0=0):
-    """V rows [n, Hkv, D] -> cache_v_b [Hkv, cap, D] at pos0.. (no norm in the configs)."""
+def fill_v_cache(cache_v_b, v_rows_u16, pos0=0, cfg=None):
+    """V rows [n, Hkv, D] -> cache_v_b [Hkv, cap, D] at pos0..: as they are (the benchmark
+    configurations), or through the product's weightless RMSNorm when cfg.v_norm (the reference
+    model's layers, docs/B6_3_attention.md:25)."""
+    from apex_b200 import ops
     n = v_rows_u16.shape[0]
     if n == 0:
+        return
+    if cfg is not None and cfg.v_norm:
+        cap, D = cache_v_b.shape[-2], cfg.head_dim
+        ops.head_norm_rope(to_dev_bf16(v_rows_u16), None, False, cache_v_b[:, pos0:, :], n, cfg.kv_heads, D, 0,
+                           cfg.rope_theta, pos0, D, cap * D, cfg.eps)
         return
     cache_v_b[:, pos0:pos0 + n, :] = to_dev_bf16(v_rows_u16).permute(1, 0, 2)
 

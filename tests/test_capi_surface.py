@@ -93,9 +93,16 @@ def test_prefill_rejects_capacity_and_workspace_errors():
 def test_decode_rejects_bad_shapes_without_gpu():
     lib = _native.load()
     f = 0x1000
-    p = _params(q_heads=16, kv_heads=4)   # group 4: not built
-    assert lib.apex_attn_decode_bf16(ctypes.byref(p), f, f, f, None, None, f, f, 1024, f, 1, 1024, f, f, 1 << 30,
-                                     None) == _native.APEX_ERR_UNSUPPORTED
+    for kw in (dict(q_heads=32, kv_heads=2), dict(head_dim=128)):   # group 16, head_dim 128: not built
+        p = _params(**kw)
+        assert lib.apex_attn_decode_bf16(ctypes.byref(p), f, f, f, None, None, f, f, 1024, f, 1, 1024, f, f,
+                                         1 << 30, None) == _native.APEX_ERR_UNSUPPORTED
+    # the wide-group / head_dim 512 form checks its arguments before touching a GPU
+    p = _params(q_heads=16, kv_heads=2, head_dim=512, rope_pairs=64)
+    assert lib.apex_attn_decode_bf16(ctypes.byref(p), f, f, f, None, None, f, f, 512, f, 1, 1024, f, f, 1 << 30,
+                                     None) == _native.APEX_ERR_INVALID_ARGUMENT   # max_seq_len > capacity
+    assert lib.apex_attn_decode_bf16(ctypes.byref(p), f, f, f, None, None, f, f, 1024, f, 1, 1024, f, f, 64,
+                                     None) == _native.APEX_ERR_WORKSPACE
     p = _params()
     # max_seq_len beyond capacity
     assert lib.apex_attn_decode_bf16(ctypes.byref(p), f, f, f, None, None, f, f, 512, f, 1, 1024, f, f, 1 << 30,

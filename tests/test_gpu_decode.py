@@ -33,7 +33,7 @@ def build_decode(cfg, seqs, lens, cap=None):
     v_new = np.stack([I.v_rows(cfg, b, L - 1, L)[0] for b, L in zip(seqs, lens)])
     for i, (b, L) in enumerate(zip(seqs, lens)):
         fill_k_cache(kc[i], I.k_rows(cfg, b, 0, L - 1), kw, cfg)
-        fill_v_cache(vc[i], I.v_rows(cfg, b, 0, L - 1))
+        fill_v_cache(vc[i], I.v_rows(cfg, b, 0, L - 1), cfg=cfg)
     t = dict(q_raw=to_dev_bf16(q_raw), k_new=to_dev_bf16(k_new), v_new=to_dev_bf16(v_new),
              qw=to_dev_bf16(qw), kw=to_dev_bf16(kw), cache=ops.KvCache(kc, vc),
              lens=torch.tensor(np.asarray(lens, np.int32), device="cuda"), max_len=int(max(lens)))

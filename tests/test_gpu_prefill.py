@@ -18,9 +18,9 @@ pytestmark = pytest.mark.gpu
 MAN = manifest()
 
 
-def run_prefill(cfg, seqs, T_total, chunk, cap=None):
+def run_prefill(cfg, seqs, T_total, chunk, cap=None, device_out=False):
     """Prefill config sequences `seqs` over positions 0..T_total-1 in chunks; returns
-    (out f32 numpy [B, T_total, Hq, D], cache)."""
+    (out f32 numpy [B, T_total, Hq, D] -- or the bf16 device tensor with device_out -- , cache)."""
     B = len(seqs)
     Hq, Hkv, D = cfg.q_heads, cfg.kv_heads, cfg.head_dim
     cap = cap or T_total
@@ -40,7 +40,7 @@ def run_prefill(cfg, seqs, T_total, chunk, cap=None):
                               v[:, c0:c0 + T].contiguous(), to_dev_bf16(qw), to_dev_bf16(kw), cache, c0, o, ws)
         out[:, c0:c0 + T] = o
     ops.device_status()
-    return bf16_dev_to_f32(out), cache
+    return (out if device_out else bf16_dev_to_f32(out)), cache
 
 
 def edge_rows(T, window, extra=()):
@@ -106,6 +106,30 @@ def test_c4_chunked_prefill_rows_vs_reference_golden():
         worst = (max(worst[0], mx), max(worst[1], mn))
         i += n
     print(f"c4 rows vs golden: max {worst[0]:.2e} mean {worst[1]:.2e}")
+
+
+def test_c4_chunked_prefill_256_rows_all_sequences():
+    """The whole C4 configuration (4 x 32768 tokens in 8 chunks of 4096, appended to the cache in
+    order) with 64 sampled rows of every sequence: the first rows, every chunk edge (p0 - 1, p0,
+    p0 + 1), the last row and random rows, against the fp32 restatement (which equals the
+    reference's own CPU code bit for bit, tests/test_oracle.py)."""
+    cfg = CONFIGS["c4_chunked_prefill"]
+    S, C = cfg.seq_len, cfg.chunk
+    got, _ = run_prefill(cfg, list(range(cfg.batch)), S, C, device_out=True)
+    edges = {0, 1, 2, S - 1}
+    for p0 in range(C, S, C):
+        edges |= {p0 - 1, p0, p0 + 1}
+    rng = np.random.default_rng(4)
+    worst, n_rows = (0.0, 0.0), 0
+    for b in range(cfg.batch):
+        rest = [int(r) for r in rng.choice(S, 64 - len(edges), replace=False) if int(r) not in edges]
+        rows = sorted(edges | set(rest))
+        ref = oracle_prefill_rows(cfg, b, max(rows) + 1, rows)
+        mx, mn = assert_close(bf16_dev_to_f32(got[b, rows]), ref, f"c4 seq {b} ({len(rows)} rows)")
+        worst = (max(worst[0], mx), max(worst[1], mn))
+        n_rows += len(rows)
+    assert n_rows >= 250
+    print(f"c4 {n_rows} rows over {cfg.batch} sequences: max {worst[0]:.2e} mean {worst[1]:.2e}")
 
 
 def test_batched_prefill_equals_per_sequence():

@@ -213,3 +213,14 @@ def test_e2m1_e4m3_tables():
     assert [L.orc_e2m1(c | 8) for c in range(1, 8)] == [-0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
     assert L.orc_e4m3(0x38) == 1.0 and L.orc_e4m3(0x01) == 2.0 ** -9 and L.orc_e4m3(0x7E) == 448.0
     assert L.orc_e4m3(0xB8) == -1.0
+
+
+def test_global_layer_restatement_vs_reference_golden():
+    """Head_dim 512, partial RoPE, V norm: the restatement's decode composition against the goldens
+    the reference's own CPU code made (the reference gate, rel-L2 < 1e-5)."""
+    cfg = CONFIGS["global_decode"]
+    g = golden("global_decode")
+    for i, r in enumerate(manifest()["global_decode"]["rows"]):
+        ref, _, _ = oracle_decode_seq(cfg, r["seq"], r["context"])
+        _, rel = oracle.diff(ref, g[i])
+        assert rel < 1e-5, rel
