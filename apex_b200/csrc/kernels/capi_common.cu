@@ -111,6 +111,24 @@ int make_tensor_map_bf16_3d(CUtensorMap *map, const void *base, uint64_t d0, uin
     return APEX_OK;
 }
 
+int make_tensor_map_bf16_3d_box(CUtensorMap *map, const void *base, const uint64_t (&dims)[3],
+                                const uint64_t (&strides_bytes)[2], const uint32_t (&box)[3]) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(APEX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+    const cuuint64_t st[2] = {strides_bytes[0], strides_bytes[1]};
+    const cuuint32_t bx[3] = {box[0], box[1], box[2]};
+    const cuuint32_t estride[3] = {1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), d, st, bx, estride,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(APEX_ERR_INVALID_ARGUMENT,
+                    "cuTensorMapEncodeTiled rejected the tensor (error " + std::to_string((int)r) +
+                        "): base must be 16-byte aligned and strides multiples of 16 bytes");
+    return APEX_OK;
+}
+
 int make_tensor_map_bf16_4d_sw64(CUtensorMap *map, const void *base, const uint64_t (&dims)[4],
                                  const uint64_t (&strides_bytes)[3], const uint32_t (&box)[4]) {
     EncodeTiledFn fn = encode_fn();
@@ -135,7 +153,7 @@ extern "C" {
 
 const char *apex_cuda_last_error(void) { return apex::t_last_error.c_str(); }
 
-int apex_cuda_abi_version(void) { return 101; }
+int apex_cuda_abi_version(void) { return 102; }
 
 int apex_cuda_device_status(void *stream) {
     unsigned int host = 0;

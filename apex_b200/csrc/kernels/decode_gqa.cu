@@ -13,10 +13,14 @@
 //                                                     the scores keep ~16 mantissa bits of q)
 //   O^T [D x 8 heads]     += V^T [D x 16] . P^T     (A = V rows through ldmatrix.trans; P^T from the
 //                                                     S^T accumulator by two movmatrix.trans)
-// A CTA = 4 consumer warps + 1 producer warp.  The producer copies K and V rows with 1-D TMA bulk
-// copies, one per 1 KB row, into rows padded by 16 bytes (so ldmatrix reads are free of bank
-// conflicts) of a ring of 16-key stages; each consumer warp takes whole stages and keeps its own
-// online softmax (log2 domain) with O^T in registers (D/16 accumulator tiles).  Warps merge through
+// A CTA = 4 consumer warps + 1 producer warp.  The producer copies each 16-key stage of K and of V
+// with ONE tiled TMA copy each: a 3-D view of the cache -- 64-element (128-byte) chunks of a row,
+// rows, chunks -- with box {64, 16, D/64} lands chunk-major in shared memory ([chunk][key][128 B]),
+// and the 128-byte swizzle then XORs a key's 16-byte columns with key & 7, so the 8 rows an ldmatrix
+// reads at one column sit in 8 different bank groups.  (Per-row 1 KB bulk copies into padded rows
+// were tried first: 32 copies per stage capped the kernel at ~0.6 of HBM.)  Each consumer warp takes
+// whole stages and keeps its own online softmax (log2 domain) with O^T in registers (D/16
+// accumulator tiles).  Warps merge through
 // shared memory, splits through the workspace, the last CTA of a (sequence, kv head) merging them.
 // tcgen05 would need M >= 64 rows of one operand in shared memory per MMA and a TMEM round trip per
 // 16-key tile for the softmax; at 8 heads per step the tensor work is ~2 % of the tensor peak, so
@@ -52,11 +56,12 @@ struct GqaArgs {
 
 template <int D>
 struct GqaSmem {
-    static constexpr int kRow = D * 2 + 16;                 // padded row bytes
-    static constexpr int kStageBytes = 2 * kStagePos * kRow;  // K rows then V rows
-    static constexpr int kStages = D == 512 ? 4 : 8;         // 133 KB / 135 KB of K/V in flight
-    uint8_t ring[kStages][kStageBytes];
-    uint8_t tail[kStageBytes];                    // the new token (row 0) and 15 zero rows
+    static constexpr int kChunks = D / 64;                      // 128-byte chunks of a row
+    static constexpr int kTile = kStagePos * D * 2;             // one operand's 16 keys, swizzled
+    static constexpr int kStageBytes = 2 * kTile;               // K tile then V tile
+    static constexpr int kStages = D == 512 ? 4 : 8;            // 128 KB of K/V in flight
+    alignas(1024) uint8_t ring[kStages][kStageBytes];
+    alignas(1024) uint8_t tail[kStageBytes];      // the new token (key 0) and 15 zero keys
     uint16_t q[2][kHeads][D + 8];                 // bf16 hi / lo planes of the scaled q, padded rows
     float rope_cs[256], rope_sn[256];
     float red_m[kWarps][kHeads], red_l[kWarps][kHeads];
@@ -136,34 +141,51 @@ __device__ __forceinline__ void load_row(const uint16_t *src, uint32_t lane, flo
     }
 }
 
+// Shared-memory byte offset of key `key`, 16-byte column `col` (of D/8) in a swizzled 16-key tile:
+// chunk-major [col / 8][key][128 B] with the 16-byte column inside the chunk XORed with key & 7.
+__device__ __forceinline__ uint32_t tile_off(uint32_t key, uint32_t col) {
+    return (col >> 3) * (kStagePos * 128) + key * 128 + (((col & 7) ^ (key & 7)) << 4);
+}
+
 // One 16-key tile of this warp: scores, online softmax, O^T += V^T P^T.  kbase / vbase: shared
-// addresses of the tile's padded K / V rows; nvalid keys valid (the V rows past it are zero).
+// addresses of the tile's swizzled K / V keys; nvalid keys valid (the V keys past it are zero).
 template <int D>
 __device__ __forceinline__ void gqa_tile(uint32_t kbase, uint32_t vbase, int nvalid, uint32_t lane, uint32_t qhi,
                                          uint32_t qlo, float (&m)[2], float (&l)[2], float (&o)[D / 16][4]) {
-    constexpr int kRow = GqaSmem<D>::kRow;
     const uint32_t g = lane >> 2, c = lane & 3;
     const uint32_t mi = lane >> 3, r = lane & 7;
-    // A = K rows: matrix mi covers keys r + 8*(mi & 1), dims 8*(mi >> 1) of each 16-dim step
-    const uint32_t a_addr = kbase + (r + 8 * (mi & 1)) * kRow + 16 * (mi >> 1);
+    // A = K keys: matrix mi covers keys r + 8*(mi & 1), the 16-byte column 2*kk + (mi >> 1) of step kk
+    const uint32_t a_key = r + 8 * (mi & 1), a_col = mi >> 1;
     // B = q rows (heads): matrix (lane >> 3) & 1 covers dims 8*((lane >> 3) & 1)
     const uint32_t b_off = (lane & 7) * ((D + 8) * 2) + 16 * ((lane >> 3) & 1);
-    float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-    for (int kk = 0; kk < D / 16; ++kk) {
-        uint32_t a[4], bh0, bh1, bl0, bl1;
-        ldsm_x4(a_addr + kk * 32, a);
-        ldsm_x2(qhi + b_off + kk * 32, bh0, bh1);
-        ldsm_x2(qlo + b_off + kk * 32, bl0, bl1);
-        mma_bf16(s, a, bh0, bh1);
-        mma_bf16(s2, a, bl0, bl1);
+    // four independent accumulator pairs (hi, lo) over the 16-dim steps: eight short MMA chains
+    constexpr int kChains = 4;
+    float s[kChains][2][4];
+#pragma unroll
+    for (int ch = 0; ch < kChains; ++ch)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[ch][0][j] = s[ch][1][j] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; kk += kChains) {
+#pragma unroll
+        for (int ch = 0; ch < kChains; ++ch) {
+            uint32_t a[4], bh0, bh1, bl0, bl1;
+            ldsm_x4(kbase + tile_off(a_key, 2 * (kk + ch) + a_col), a);
+            ldsm_x2(qhi + b_off + (kk + ch) * 32, bh0, bh1);
+            ldsm_x2(qlo + b_off + (kk + ch) * 32, bl0, bl1);
+            mma_bf16(s[ch][0], a, bh0, bh1);
+            mma_bf16(s[ch][1], a, bl0, bl1);
+        }
     }
-    // s[j]: key g (j < 2) or g + 8 (j >= 2), head 2c + (j & 1)
+    // scores: key g (j < 2) or g + 8 (j >= 2), head 2c + (j & 1)
     float p[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int key = static_cast<int>(g) + (j >= 2 ? 8 : 0);
-        p[j] = key < nvalid ? s[j] + s2[j] : -INFINITY;
+        float v = 0.f;
+#pragma unroll
+        for (int ch = 0; ch < kChains; ++ch) v += s[ch][0][j] + s[ch][1][j];
+        p[j] = key < nvalid ? v : -INFINITY;
     }
     float mx[2] = {fmaxf(p[0], p[2]), fmaxf(p[1], p[3])};
 #pragma unroll
@@ -193,24 +215,27 @@ __device__ __forceinline__ void gqa_tile(uint32_t kbase, uint32_t vbase, int nva
     // P^T as the B operand: keys 0-7 and 8-15 transposed into (key = 2c.., head = g)
     const uint32_t b0 = movmatrix_t(pack_bf16(p[0], p[1]));
     const uint32_t b1 = movmatrix_t(pack_bf16(p[2], p[3]));
-    // A = V^T: matrix mi covers keys r + 8*(mi >> 1), dims 8*(mi & 1) of each 16-dim tile
-    const uint32_t v_addr = vbase + (r + 8 * (mi >> 1)) * kRow + 16 * (mi & 1);
+    // A = V^T: matrix mi covers keys r + 8*(mi >> 1), the 16-byte column 2*t + (mi & 1) of dim tile t
+    const uint32_t v_key = r + 8 * (mi >> 1), v_col = mi & 1;
 #pragma unroll
     for (int t = 0; t < D / 16; ++t) {
         uint32_t a[4];
-        ldsm_x4_t(v_addr + t * 32, a);
+        ldsm_x4_t(vbase + tile_off(v_key, 2 * t + v_col), a);
         mma_bf16(o[t], a, b0, b1);
     }
 }
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1) decode_gqa_kernel(const __grid_constant__ GqaArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) decode_gqa_kernel(const __grid_constant__ GqaArgs a,
+                                                                 const __grid_constant__ CUtensorMap tk,
+                                                                 const __grid_constant__ CUtensorMap tv) {
     using Smem = GqaSmem<D>;
     constexpr int E = D / 32;
-    constexpr int kRow = Smem::kRow;
+    constexpr int kTile = Smem::kTile;
     constexpr int ST = Smem::kStages;
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+    // the 128-byte swizzle repeats every 1024 bytes: stage tiles start on 1024-byte boundaries
+    Smem &sm = *reinterpret_cast<Smem *>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const uint32_t G = a.group;
@@ -247,19 +272,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_gqa_kernel(const __grid_co
     if (warp == kWarps) {
         // ---------------------------------------------------------------- producer
         if (lane == 0) {
+            prefetch_tensormap(&tk);
+            prefetch_tensormap(&tv);
+            // row index of this split's first key in the [B * Hkv * capacity] rows of the cache
+            const int32_t row0 = static_cast<int32_t>((static_cast<uint64_t>(b) * a.kv_heads + kvh) * a.capacity + lo);
             for (uint32_t s = 0; s < n_stages; ++s) {
                 const uint32_t slot = s % ST;
                 if (s >= ST && !mbar_wait(smem_u32(&sm.empty[slot]), ((s / ST) - 1) & 1, a.status)) break;
-                const uint32_t n = min(static_cast<uint32_t>(kStagePos), n_cached - s * kStagePos);
                 const uint32_t full = smem_u32(&sm.full[slot]);
-                mbar_arrive_expect_tx(full, 2 * n * D * 2);
-                const uint64_t row0 = head_base + static_cast<uint64_t>(lo + s * kStagePos) * D;
+                // 16 whole keys every stage (keys past the split are masked; past the cache, zero)
+                mbar_arrive_expect_tx(full, 2 * kTile);
                 const uint32_t dst = smem_u32(sm.ring[slot]);
-                for (uint32_t j = 0; j < n; ++j) {  // one 16-byte-aligned padded row per copy
-                    tma_bulk_load(dst + j * kRow, a.k_cache + row0 + static_cast<uint64_t>(j) * D, D * 2, full);
-                    tma_bulk_load(dst + (kStagePos + j) * kRow, a.v_cache + row0 + static_cast<uint64_t>(j) * D, D * 2,
-                                  full);
-                }
+                tma_load_3d(dst, &tk, 0, row0 + static_cast<int32_t>(s * kStagePos), 0, full);
+                tma_load_3d(dst + kTile, &tv, 0, row0 + static_cast<int32_t>(s * kStagePos), 0, full);
             }
         }
         return;
@@ -299,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_gqa_kernel(const __grid_co
         else
             norm_rope_row<D>(x, lane, a.v_norm, nullptr, a.eps, 0, sm.rope_cs, sm.rope_sn);
         uint16_t *dst = (is_k ? a.k_cache : a.v_cache) + head_base + static_cast<uint64_t>(pos_new) * D;
-        uint8_t *trow = sm.tail + (is_k ? 0 : kStagePos * kRow);
+        uint8_t *ttile = sm.tail + (is_k ? 0 : kTile);
 #pragma unroll
         for (int k = 0; k < E / 8; ++k) {
             uint4 pk;
@@ -308,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_gqa_kernel(const __grid_co
             pk.z = pack_bf16(x[8 * k + 4], x[8 * k + 5]);
             pk.w = pack_bf16(x[8 * k + 6], x[8 * k + 7]);
             *reinterpret_cast<uint4 *>(dst + E * lane + 8 * k) = pk;
-            *reinterpret_cast<uint4 *>(trow + (E * lane + 8 * k) * 2) = pk;
+            *reinterpret_cast<uint4 *>(ttile + tile_off(0, (E * lane + 8 * k) / 8)) = pk;  // key 0
         }
     }
     gqa_sync();
@@ -323,19 +348,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_gqa_kernel(const __grid_co
         if (!mbar_wait(smem_u32(&sm.full[slot]), (s / ST) & 1, a.status)) break;
         const int n = static_cast<int>(min(static_cast<uint32_t>(kStagePos), n_cached - s * kStagePos));
         uint8_t *st = sm.ring[slot];
-        if (n < kStagePos) {  // rows past the copied ones may hold non-finite bits: zero V's
+        if (n < kStagePos) {  // keys past the split's (other positions, or unwritten memory): zero V's
             for (uint32_t i = lane; i < static_cast<uint32_t>(kStagePos - n) * (D / 8); i += 32) {
-                const uint32_t row = n + i / (D / 8), col = i % (D / 8);
-                *reinterpret_cast<uint4 *>(st + (kStagePos + row) * kRow + col * 16) = make_uint4(0, 0, 0, 0);
+                const uint32_t key = n + i / (D / 8), col = i % (D / 8);
+                *reinterpret_cast<uint4 *>(st + kTile + tile_off(key, col)) = make_uint4(0, 0, 0, 0);
             }
             __syncwarp();
         }
-        gqa_tile<D>(smem_u32(st), smem_u32(st + kStagePos * kRow), n, lane, qhi, qlo, m, l, o);
+        gqa_tile<D>(smem_u32(st), smem_u32(st + kTile), n, lane, qhi, qlo, m, l, o);
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&sm.empty[slot]));
     }
     if (has_new && warp == 0)
-        gqa_tile<D>(smem_u32(sm.tail), smem_u32(sm.tail + kStagePos * kRow), 1, lane, qhi, qlo, m, l, o);
+        gqa_tile<D>(smem_u32(sm.tail), smem_u32(sm.tail + kTile), 1, lane, qhi, qlo, m, l, o);
 
     // ---- per-warp totals: l summed over the lanes that share heads (2c, 2c+1)
 #pragma unroll
@@ -480,6 +505,7 @@ int launch_gqa_decode(const apex_attn_params *p, const uint16_t *q_raw, const ui
                       const uint16_t *q_w, const uint16_t *k_w, uint16_t *k_cache, uint16_t *v_cache,
                       uint32_t capacity, const int32_t *seq_lens, uint32_t batch, uint32_t max_seq_len,
                       uint16_t *out, void *workspace, size_t workspace_bytes_given, void *stream, const char *name) {
+    if (p->ring) return fail(APEX_ERR_UNSUPPORTED, std::string(name) + ": ring caches are served for head_dim 256, group 2");
     if (batch == 0) return ok();
     if (batch > 65535 || p->kv_heads > 65535) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": batch or kv_heads too large");
     if (p->rope_pairs > p->head_dim / 2)
@@ -516,21 +542,32 @@ int launch_gqa_decode(const apex_attn_params *p, const uint16_t *q_raw, const ui
         grid_x = (range + a.chunk - 1) / a.chunk;
     }
     rope_table(a.rope.inv_freq, p->rope_pairs, p->head_dim, p->rope_base);
+    // the caches as {64 elements, rows, D/64 chunks} with byte strides {D*2, 128}: one box = 16 keys
+    // of one operand, chunk-major in shared memory
+    const uint64_t rows = static_cast<uint64_t>(batch) * p->kv_heads * capacity;
+    if (rows > 0x7fffffffull) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": cache too large");
+    const uint64_t dims[3] = {64, rows, p->head_dim / 64u};
+    const uint64_t strides[2] = {p->head_dim * 2ull, 128};
+    const uint32_t box[3] = {64, static_cast<uint32_t>(kStagePos), p->head_dim / 64u};
+    CUtensorMap tk, tv;
+    int rc = make_tensor_map_bf16_3d_box(&tk, k_cache, dims, strides, box);
+    if (rc) return rc;
+    rc = make_tensor_map_bf16_3d_box(&tv, v_cache, dims, strides, box);
+    if (rc) return rc;
     const dim3 grid(grid_x, p->kv_heads, batch);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    int rc;
     if (p->head_dim == 512) {
         rc = check_cuda(cudaFuncSetAttribute(decode_gqa_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(sizeof(GqaSmem<512>))),
+                                             static_cast<int>(sizeof(GqaSmem<512>) + 1024)),
                         name);
         if (rc) return rc;
-        decode_gqa_kernel<512><<<grid, kThreads, sizeof(GqaSmem<512>), s>>>(a);
+        decode_gqa_kernel<512><<<grid, kThreads, sizeof(GqaSmem<512>) + 1024, s>>>(a, tk, tv);
     } else {
         rc = check_cuda(cudaFuncSetAttribute(decode_gqa_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(sizeof(GqaSmem<256>))),
+                                             static_cast<int>(sizeof(GqaSmem<256>) + 1024)),
                         name);
         if (rc) return rc;
-        decode_gqa_kernel<256><<<grid, kThreads, sizeof(GqaSmem<256>), s>>>(a);
+        decode_gqa_kernel<256><<<grid, kThreads, sizeof(GqaSmem<256>) + 1024, s>>>(a, tk, tv);
     }
     rc = check_cuda(cudaGetLastError(), name);
     return rc ? rc : ok();

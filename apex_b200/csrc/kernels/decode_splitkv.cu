@@ -64,6 +64,7 @@ struct DecodeArgs {
     unsigned *status;    // device status word
     uint32_t capacity, q_heads, kv_heads, rope_pairs, window, qk_norm, v_norm;
     uint32_t chunk, max_splits, kv_begin, kv_end, max_seq_len;
+    uint32_t ring;       // 1: position p of the cache is slot p % capacity (window <= capacity)
     float rope_base, eps, scale_log2;
     int partial_mode;
     // peer mode (a KV range split over `world` GPUs): this rank's partial goes straight into every
@@ -400,7 +401,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CL && ST > 1) ? 1 : 2)
     // ---- key range of this (b, kv head) and of this split (global positions)
     const int32_t L = a.seq_lens[b];
     const bool bad = L < 0 || static_cast<uint32_t>(L) > a.max_seq_len ||
-                     (L > 0 && static_cast<uint32_t>(L) - 1 >= a.kv_begin + a.capacity &&
+                     (!a.ring && L > 0 && static_cast<uint32_t>(L) - 1 >= a.kv_begin + a.capacity &&
                       static_cast<uint32_t>(L) - 1 < a.kv_end);
     const uint32_t Lu = bad ? 0u : static_cast<uint32_t>(L);
     const uint32_t pos_new = Lu - 1;  // only meaningful when Lu >= 1
@@ -433,6 +434,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CL && ST > 1) ? 1 : 2)
 
     const uint16_t *kc = a.k_cache + head_base + static_cast<uint64_t>(lo - a.kv_begin) * kD;
     const uint16_t *vc = a.v_cache + head_base + static_cast<uint64_t>(lo - a.kv_begin) * kD;
+    const uint32_t new_slot = a.ring ? pos_new % a.capacity : pos_new - a.kv_begin;
 
     if (warp == CW) {
         // ---------------------------------------------------------------- producer
@@ -445,8 +447,19 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CL && ST > 1) ? 1 : 2)
                 const uint32_t bytes = n * kRowBytes;
                 const uint32_t full = smem_u32(&sm.full[slot]);
                 mbar_arrive_expect_tx(full, 2 * bytes);
-                tma_bulk_load(smem_u32(sm.k[slot]), kc + static_cast<uint64_t>(p0) * kD, bytes, full);
-                tma_bulk_load(smem_u32(sm.v[slot]), vc + static_cast<uint64_t>(p0) * kD, bytes, full);
+                if (!a.ring) {
+                    tma_bulk_load(smem_u32(sm.k[slot]), kc + static_cast<uint64_t>(p0) * kD, bytes, full);
+                    tma_bulk_load(smem_u32(sm.v[slot]), vc + static_cast<uint64_t>(p0) * kD, bytes, full);
+                } else {  // slots (lo + p0) % capacity onward, in two runs where the ring wraps
+                    const uint32_t i0 = (lo + p0) % a.capacity, n1 = min(n, a.capacity - i0);
+                    const uint16_t *kr = a.k_cache + head_base, *vr = a.v_cache + head_base;
+                    tma_bulk_load(smem_u32(sm.k[slot]), kr + static_cast<uint64_t>(i0) * kD, n1 * kRowBytes, full);
+                    tma_bulk_load(smem_u32(sm.v[slot]), vr + static_cast<uint64_t>(i0) * kD, n1 * kRowBytes, full);
+                    if (n1 < n) {
+                        tma_bulk_load(smem_u32(sm.k[slot]) + n1 * kRowBytes, kr, (n - n1) * kRowBytes, full);
+                        tma_bulk_load(smem_u32(sm.v[slot]) + n1 * kRowBytes, vr, (n - n1) * kRowBytes, full);
+                    }
+                }
             }
         }
         if constexpr (CL) {  // both cluster barrier phases, like every thread of the cluster
@@ -496,8 +509,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CL && ST > 1) ? 1 : 2)
             norm_rope_row_tab(x, lane, a.v_norm, wv, a.eps, 0, sm.rope_cs, sm.rope_sn);
         const uint4 packed = pack8(x);
         *reinterpret_cast<uint4 *>((is_k ? sm.new_k : sm.new_v) + 8 * lane) = packed;
-        uint16_t *dst = (is_k ? a.k_cache : a.v_cache) + head_base +
-                        static_cast<uint64_t>(pos_new - a.kv_begin) * kD;
+        uint16_t *dst = (is_k ? a.k_cache : a.v_cache) + head_base + static_cast<uint64_t>(new_slot) * kD;
         *reinterpret_cast<uint4 *>(dst + 8 * lane) = packed;
     }
     consumer_sync<CW>();
@@ -926,8 +938,15 @@ int plan_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t
         if (!aligned16(ptr)) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": tensors must be 16-byte aligned");
     if (max_seq_len == 0) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": max_seq_len must be >= 1");
     if (kv_end <= kv_begin) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": empty kv range");
-    const uint32_t range_len = std::min<uint32_t>(kv_end, max_seq_len) - std::min(kv_begin, max_seq_len);
-    if ((partial_mode ? static_cast<uint64_t>(kv_end) - kv_begin : max_seq_len) > capacity)
+    const bool ring = p->ring != 0;
+    if (ring && (partial_mode || peer))
+        return fail(APEX_ERR_UNSUPPORTED, std::string(name) + ": ring caches are served by the one-GPU decode only");
+    if (ring && (p->window == 0 || p->window > capacity))
+        return fail(APEX_ERR_INVALID_ARGUMENT,
+                    std::string(name) + ": a ring cache needs 0 < window <= capacity (it holds the last capacity keys)");
+    uint32_t range_len = std::min<uint32_t>(kv_end, max_seq_len) - std::min(kv_begin, max_seq_len);
+    if (!partial_mode && p->window) range_len = std::min(range_len, p->window);  // keys one query can see
+    if (!ring && (partial_mode ? static_cast<uint64_t>(kv_end) - kv_begin : max_seq_len) > capacity)
         return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": key range exceeds cache capacity");
     const size_t need = workspace_bytes(batch, p->q_heads, p->kv_heads, max_seq_len);
     if (!workspace || workspace_bytes_given < need)
@@ -950,6 +969,7 @@ int plan_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t
     a.chunk = choose_chunk(batch, p->kv_heads, range_len);
     a.max_splits = max_splits;
     a.kv_begin = kv_begin; a.kv_end = kv_end; a.max_seq_len = max_seq_len;
+    a.ring = ring ? 1u : 0u;
     a.rope_base = p->rope_base; a.eps = p->eps; a.scale_log2 = p->scale * kLog2e;
     a.partial_mode = partial_mode ? 1 : 0;
     if (peer) {
@@ -1126,6 +1146,58 @@ extern "C" int apex_attn_merge_partials(const float *partials, uint32_t num_part
     merge_partials_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(partials, num_partials,
                                                                               rows, head_dim, out);
     const int rc = check_cuda(cudaGetLastError(), "apex_attn_merge_partials");
+    return rc ? rc : ok();
+}
+
+// ---------------------------------------------------------------- ring caches
+namespace apex {
+namespace {
+
+// Rows [first, length) of linear [B][H][lin_cap][D] into ring [B][H][ring_cap][D] at slot p % ring_cap;
+// one 16-byte piece per thread.
+__global__ void kv_ring_store_kernel(const uint4 *__restrict__ k_lin, const uint4 *__restrict__ v_lin,
+                                     uint4 *__restrict__ k_ring, uint4 *__restrict__ v_ring, uint32_t heads,
+                                     uint32_t pieces, uint32_t lin_cap, uint32_t ring_cap, uint32_t first,
+                                     uint32_t n) {
+    const uint64_t total = static_cast<uint64_t>(heads) * n * pieces;  // this block row's sequence: blockIdx.y
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t c = static_cast<uint32_t>(i % pieces);
+        const uint64_t rest = i / pieces;
+        const uint32_t j = static_cast<uint32_t>(rest % n);
+        const uint64_t bh = static_cast<uint64_t>(blockIdx.y) * heads + rest / n;
+        const uint32_t pos = first + j;
+        const uint64_t src = (bh * lin_cap + pos) * pieces + c, dst = (bh * ring_cap + pos % ring_cap) * pieces + c;
+        k_ring[dst] = k_lin[src];
+        v_ring[dst] = v_lin[src];
+    }
+}
+
+}  // namespace
+}  // namespace apex
+
+extern "C" int apex_kv_ring_store(const uint16_t *k_linear, const uint16_t *v_linear, uint16_t *k_ring,
+                                  uint16_t *v_ring, uint32_t batch, uint32_t kv_heads, uint32_t head_dim,
+                                  uint32_t linear_capacity, uint32_t ring_capacity, uint32_t length, void *stream) {
+    using namespace apex;
+    const char *name = "apex_kv_ring_store";
+    if (batch == 0 || kv_heads == 0 || length == 0) return ok();
+    if (!k_linear || !v_linear || !k_ring || !v_ring) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": null tensor");
+    if (head_dim == 0 || head_dim % 8) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": head_dim a multiple of 8");
+    if (ring_capacity == 0 || length > linear_capacity)
+        return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": need ring_capacity > 0 and length <= linear_capacity");
+    for (const void *ptr : {(const void *)k_linear, (const void *)v_linear, (const void *)k_ring, (const void *)v_ring})
+        if (!aligned16(ptr)) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": tensors must be 16-byte aligned");
+    if (batch > 65535) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": batch > 65535");
+    const uint32_t first = length > ring_capacity ? length - ring_capacity : 0;
+    const uint32_t n = length - first;
+    const uint64_t per_seq = static_cast<uint64_t>(kv_heads) * n * (head_dim / 8);
+    const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((per_seq + 255) / 256, 65535));
+    kv_ring_store_kernel<<<dim3(blocks, batch), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const uint4 *>(k_linear), reinterpret_cast<const uint4 *>(v_linear),
+        reinterpret_cast<uint4 *>(k_ring), reinterpret_cast<uint4 *>(v_ring), kv_heads, head_dim / 8, linear_capacity,
+        ring_capacity, first, n);
+    const int rc = check_cuda(cudaGetLastError(), name);
     return rc ? rc : ok();
 }
 

@@ -28,6 +28,12 @@ int make_tensor_map_bf16_3d(CUtensorMap *map, const void *base, uint64_t d0, uin
                             uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
                             uint32_t box0, uint32_t box1);
 
+// A 3-D bf16 tensor map with 128-byte swizzle and a full 3-D box: dims {d0 (innermost, elements),
+// d1, d2}, byte strides of dims 1 and 2 (any order), box {box0, box1, box2}.  Out-of-range elements read
+// as zero.
+int make_tensor_map_bf16_3d_box(CUtensorMap *map, const void *base, const uint64_t (&dims)[3],
+                                const uint64_t (&strides_bytes)[2], const uint32_t (&box)[3]);
+
 // A 4-D bf16 tensor map with 64-byte swizzle, for tiled stores of 32-element (64-byte) rows:
 // dims {d0 (innermost), d1, d2, d3}, byte strides of dims 1..3, box {box0, box1, box2, box3}.
 // Elements outside the tensor are not written.

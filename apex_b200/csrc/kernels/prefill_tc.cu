@@ -862,6 +862,7 @@ int validate_prefill(const apex_attn_params *p, uint32_t capacity, uint32_t batc
     const std::string n(name);
     if (!p) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": null params");
     if (p->head_dim != kD) return fail(APEX_ERR_UNSUPPORTED, n + ": this build supports head_dim 256");
+    if (p->ring) return fail(APEX_ERR_UNSUPPORTED, n + ": prefill writes a linear cache (copy its last keys into a ring with apex_kv_ring_store)");
     if (p->kv_heads == 0 || p->q_heads == 0 || p->q_heads % p->kv_heads)
         return fail(APEX_ERR_INVALID_ARGUMENT, n + ": q_heads must be a multiple of kv_heads");
     if (p->rope_pairs > kD / 2) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": rope_pairs > head_dim / 2");

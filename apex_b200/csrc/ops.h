@@ -116,9 +116,9 @@ struct KvCacheBf16 {
 
 // Numerics of the bf16 operators (apex_attn_params); scale defaults to 1/sqrt(head_dim).
 inline apex_attn_params attnParams(const AttentionShape &s, float scale, float eps, bool qk_norm,
-                                   bool v_norm) {
+                                   bool v_norm, bool ring = false) {
     return apex_attn_params{s.q_heads, s.kv_heads, s.head_dim, s.rope_pairs, s.rope_base, s.window,
-                            scale, eps, qk_norm ? 1u : 0u, v_norm ? 1u : 0u};
+                            scale, eps, qk_norm ? 1u : 0u, v_norm ? 1u : 0u, ring ? 1u : 0u};
 }
 
 // Bytes of the workspace attentionDecodeBf16 / attentionPrefillBf16 need.

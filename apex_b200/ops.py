@@ -40,11 +40,12 @@ class AttentionShape:
     eps: float = 1e-6
     qk_norm: bool = True
     v_norm: bool = False
+    ring: bool = False            # decode: the cache is a ring of `capacity` slots (position % capacity)
 
     def c(self) -> AttnParams:
         return AttnParams(self.q_heads, self.kv_heads, self.head_dim, self.rope_pairs,
                           self.rope_base, self.window, self.scale, self.eps, int(self.qk_norm),
-                          int(self.v_norm))
+                          int(self.v_norm), int(self.ring))
 
     @staticmethod
     def from_config(cfg) -> "AttentionShape":
@@ -215,6 +216,20 @@ def attention_decode_kvsplit(shape: AttentionShape, q_raw, k_new, v_new, q_norm_
                                             ctypes.byref(exchange), out.data_ptr(),
                                             workspace.buffer.data_ptr(), workspace.nbytes, _stream()))
     return out
+
+
+def kv_ring_store(linear: KvCache, ring: KvCache, length: int) -> KvCache:
+    """Copy the last min(length, ring capacity) positions of a linear bf16 cache [B, Hkv, cap, D]
+    into a ring cache [B, Hkv, R, D] (position p at slot p % R), apex_kv_ring_store."""
+    for t, n in ((linear.k, "linear.k"), (linear.v, "linear.v"), (ring.k, "ring.k"), (ring.v, "ring.v")):
+        _need(t, torch.bfloat16, n)
+    B, H, _, D = linear.k.shape
+    if ring.k.shape[0] != B or ring.k.shape[1] != H or ring.k.shape[3] != D:
+        raise ValueError("kv_ring_store: ring must be [B, Hkv, R, D] like the linear cache")
+    check(_native.load().apex_kv_ring_store(linear.k.data_ptr(), linear.v.data_ptr(), ring.k.data_ptr(),
+                                            ring.v.data_ptr(), B, H, D, linear.capacity, ring.capacity, length,
+                                            _stream()))
+    return ring
 
 
 def merge_partials(partials: torch.Tensor, out: torch.Tensor) -> torch.Tensor:

@@ -13,9 +13,12 @@ memory (one launch per step; NCCL all-gather + merge kernel when peer mapping is
 Every other configuration is measured in the same run and reported under "workloads" (same
 fields): c1_decode, c2_prefill_window (one fused prefill = prep + tcgen05 attention),
 c3_ragged_decode, c4_chunked_prefill (one step = the whole 32768-token prefill of 4 sequences in
-8 chunks of 4096 appended to the cache in order) and c5_long_decode_b1.  At N > 1: c1 / c2 run
-replicas (weak scaling); c3 shards sequences; c4 shards sequences where the batch divides over
-the GPUs and kv heads otherwise; c5 splits the KV sequence (strong scaling).
+8 chunks of 4096 appended to the cache in order), c5_long_decode_b1, global_decode (the reference
+model's global layers: 8 decodes over 32768 keys of 2 kv heads of head_dim 512, GQA group 8, RoPE on
+64 pairs, V norm) and proj_decode (the NVFP4 q/k/v projections and o_proj + post-attention RMSNorm of
+one decode token).  At N > 1: c1 / c2 / proj run replicas (weak scaling); c3 and global_decode shard
+sequences; c4 shards sequences where the batch divides over the GPUs and kv heads otherwise; c5 splits
+the KV sequence (strong scaling).
 
 Timing: W warm-up steps; then EXACTLY K steps replayed from CUDA graphs over rotating input sets
 (more bytes than the 126 MB L2 between reuses), bracketed by barrier + synchronize, CUDA events on
@@ -54,7 +57,7 @@ from apex_b200.configs import CONFIGS, decode_bytes, prefill_flops, visible_pair
 
 PRIMARY = "c5_long_decode_b8"
 ALSO = ("c1_decode", "c2_prefill_window", "c3_ragged_decode", "c4_chunked_prefill", "c5_long_decode_b1",
-        "proj_decode")
+        "global_decode", "proj_decode")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_BYTES = 126 * 1024 * 1024
 TOL_MAX, TOL_MEAN = 2e-2, 2e-3          # against an fp32 reference
@@ -327,8 +330,9 @@ class DecodeWorkload:
         else:
             lens_all = [cfg.context] * cfg.batch
         self.kv_split = cfg.name.startswith("c5") and world > 1
-        mine = adist.shard_sequences(lens_all, world)[rank] if (cfg.lens_range and world > 1) else list(range(cfg.batch))
-        self.sharding = "kv-split" if self.kv_split else "batch-shard" if (cfg.lens_range and world > 1) else "replica"
+        batch_shard = not self.kv_split and world > 1 and cfg.batch >= world
+        mine = adist.shard_sequences(lens_all, world)[rank] if batch_shard else list(range(cfg.batch))
+        self.sharding = "kv-split" if self.kv_split else "batch-shard" if batch_shard else "replica"
         self.lens = [lens_all[i] for i in mine]
         self.all_lens = lens_all
         B = len(self.lens)

@@ -51,7 +51,8 @@ extern "C" {
  *   qk_norm  1: RMSNorm q and k over head_dim (weights optional), 0: no norm
  *   v_norm   1: weightless RMSNorm of v (the reference model, docs/B6_3_attention.md:25)
  *   window   0 = global causal; else key j is visible to the query at position p iff
- *            p - window < j <= p (docs/B6_3_attention.md:42)                              */
+ *            p - window < j <= p (docs/B6_3_attention.md:42)
+ *   ring     see the field                                                                 */
 typedef struct apex_attn_params {
     uint32_t q_heads;
     uint32_t kv_heads;
@@ -63,6 +64,9 @@ typedef struct apex_attn_params {
     float eps;
     uint32_t qk_norm;
     uint32_t v_norm;
+    uint32_t ring;       /* decode only: 1 = the cache is a ring of `capacity` slots, position p at slot
+                            p % capacity (the reference's planned sliding-layer cache,
+                            docs/B6_3_attention.md:99-102); needs 0 < window <= capacity.  0 = linear. */
 } apex_attn_params;
 
 /* Message of the last failing call on this host thread ("" if none). */
@@ -124,8 +128,11 @@ APEX_API int apex_attn_decode_workspace_init(void *workspace, size_t workspace_b
  *   K[b][:, L-1] = rope(rmsnorm(k_new[b], k_norm_w)), V[b][:, L-1] = [rmsnorm](v_new[b])
  *   out[b] = softmax(scale * q K^T) V over the visible keys          (split-KV, LSE merge)
  * q_raw [B][Hq][D]; k_new, v_new [B][Hkv][D]; caches [B][Hkv][capacity][D]; seq_lens is a
- * DEVICE int32 [B] with 1 <= seq_lens[b] <= max_seq_len <= capacity; out [B][Hq][D].
- * Norm weights are bf16 [D] or NULL (weight 1.0).  head_dim 256, Hq / Hkv = 2. */
+ * DEVICE int32 [B] with 1 <= seq_lens[b] <= max_seq_len <= capacity (a ring cache: any max_seq_len,
+ * window <= capacity); out [B][Hq][D].  Norm weights are bf16 [D] or NULL (weight 1.0).
+ * head_dim 256 with Hq / Hkv = 2 (split-KV kernel; short contexts of small batches as thread-block
+ * clusters), or head_dim 256 / 512 with 1..8 q heads per kv head (tensor-core decode of the
+ * reference model's global layers; linear caches). */
 APEX_API int apex_attn_decode_bf16(const apex_attn_params *p, const uint16_t *q_raw,
                           const uint16_t *k_new, const uint16_t *v_new,
                           const uint16_t *q_norm_w, const uint16_t *k_norm_w,
@@ -155,6 +162,14 @@ APEX_API int apex_attn_decode_bf16_noalloc(const apex_attn_params *p, const uint
                                            uint16_t *k_cache, uint16_t *v_cache, uint32_t capacity,
                                            const int32_t *seq_lens, uint32_t batch,
                                            uint32_t max_seq_len, uint16_t *out, void *stream);
+
+/* Ring caches (apex_attn_params.ring): copies the last min(length, ring_capacity) positions of a linear
+ * cache [batch][kv_heads][linear_capacity][head_dim] (e.g. what a prefill wrote) into a ring
+ * [batch][kv_heads][ring_capacity][head_dim], position p at slot p % ring_capacity -- the reference's
+ * planned 1024-entry sliding-layer cache (docs/B6_3_attention.md:99-102).  bf16 bits; 16-byte aligned. */
+APEX_API int apex_kv_ring_store(const uint16_t *k_linear, const uint16_t *v_linear, uint16_t *k_ring, uint16_t *v_ring,
+                                uint32_t batch, uint32_t kv_heads, uint32_t head_dim, uint32_t linear_capacity,
+                                uint32_t ring_capacity, uint32_t length, void *stream);
 
 /* KV-sequence-split decode: this caller holds global key positions [kv_begin, kv_end) of
  * every sequence, stored at local cache index (position - kv_begin).  Same fused step as

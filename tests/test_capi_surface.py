@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared():
         assert name in syms, name
         assert getattr(lib, name) is not None
-    assert lib.apex_cuda_abi_version() == 101
+    assert lib.apex_cuda_abi_version() == 102
 
 
 def _params(**kw):
@@ -119,3 +119,22 @@ def test_f32_dropins_reject_bad_head_dim():
                                        None) == _native.APEX_ERR_INVALID_ARGUMENT
     assert lib.apex_attention_f32(f, f, f, f, 1, 16, 8, 1024, 4, 0, 0, None) == _native.APEX_ERR_INVALID_ARGUMENT
     assert lib.apex_attention_f32(f, f, f, f, 4, 16, 8, 64, 4, 1, 0, None) == _native.APEX_ERR_INVALID_ARGUMENT
+
+
+def test_ring_rejections():
+    lib = _native.load()
+    f = 0x1000
+    import dataclasses
+    from apex_b200 import ops
+    base = ops.AttentionShape(16, 8, 256, 128, 1e4, 0, 1 / 16, 1e-6, True, False, True)
+    for window, code in ((0, _native.APEX_ERR_INVALID_ARGUMENT), (2048, _native.APEX_ERR_INVALID_ARGUMENT)):
+        p = dataclasses.replace(base, window=window).c()
+        import ctypes
+        assert lib.apex_attn_decode_bf16(ctypes.byref(p), f, f, f, None, None, f, f, 1024, f, 1, 9000, f, f, 1 << 30,
+                                         None) == code
+    p = dataclasses.replace(base, window=1024).c()
+    import ctypes
+    assert lib.apex_attn_decode_partial_bf16(ctypes.byref(p), f, f, f, None, None, f, f, 1024, f, 1, 9000, 0, 4096, f,
+                                             f, 1 << 30, None) == _native.APEX_ERR_UNSUPPORTED
+    assert lib.apex_attn_prefill_bf16(ctypes.byref(p), f, f, f, None, None, f, f, 1024, 1, 16, 0, f, f, 1 << 30,
+                                      None) == _native.APEX_ERR_UNSUPPORTED
