@@ -1,9 +1,11 @@
 """Multi-GPU host logic of the attention path: one process per GPU over torch.distributed.
 
-Only two shardings exist, where the work splits naturally:
+Only these shardings exist, where the work splits naturally:
 
-* batch sharding (ragged decode, chunked prefill): whole sequences go to ranks, balanced by
-  key count (longest first onto the least-loaded rank); no collective on the data path.
+* batch sharding (ragged decode, batched decode, chunked prefill when the batch divides over the
+  ranks): whole sequences go to ranks, balanced by key count (longest first onto the least-loaded
+  rank); no collective on the data path.  A chunked prefill whose batch does not divide (4
+  sequences over 8 GPUs) shards kv heads with their q heads instead, also with no collective.
 * KV-sequence split (one long decode): rank r holds key positions [begin_r, end_r) of every
   sequence.  Fused form (PeerExchangeBuffers + apex_attn_decode_kvsplit_bf16): the decode
   kernel writes each rank's partial (o, m, l) straight into every rank's gather buffer over

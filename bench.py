@@ -385,7 +385,10 @@ class DecodeWorkload:
         owns_tokens = not self.kv_split or rank == 0
         self.tokens = B if owns_tokens else 0
         self.launches_per_step = 2 if self.kv_split and self.peer is None else 1
-        self.kernel_name = "decode_kernel" + (" (partial mode, this rank's key range)" if self.kv_split else "")
+        # head_dim 512 or a GQA group other than 2 runs the tensor-core decode (decode_gqa.cu)
+        gqa_form = cfg.head_dim != 256 or Hq != 2 * Hkv
+        self.kernel_name = ("decode_gqa_kernel" if gqa_form else "decode_kernel") + (
+            " (partial mode, this rank's key range)" if self.kv_split else "")
 
     def _call(self, s):
         if self.peer is not None:

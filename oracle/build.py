@@ -10,6 +10,9 @@ Two shared libraries:
   ``oracle/_ref/doc_cpu_ref_additions.h`` at build time.  Built only when the reference tree
   is present; the result is git-ignored and travels with the working tree.
 
+The reference tree is ``--reference DIR``, else ``$APEX_REFERENCE_DIR``, else a checkout named
+``reference`` beside this repository's directory.
+
 Usage: ``python oracle/build.py [--reference DIR]``.
 """
 from __future__ import annotations
@@ -23,7 +26,8 @@ import sys
 HERE = pathlib.Path(__file__).resolve().parent
 BUILD = HERE / "_build"
 REF_OUT = HERE / "_ref"
-DEFAULT_REFERENCE_DIR = "/root/reference"
+# a reference checkout beside this repository (overridden by --reference / $APEX_REFERENCE_DIR)
+SIBLING_REFERENCE_DIR = HERE.parent.parent / "reference"
 
 ORACLE_LIB = BUILD / "liboracle.so"
 REF_LIB = REF_OUT / "libapexref.so"
@@ -61,7 +65,7 @@ def extract_doc_block(doc_path: pathlib.Path) -> str:
 
 
 def build_reference(reference_dir: str | os.PathLike | None = None) -> pathlib.Path | None:
-    ref = pathlib.Path(reference_dir or os.environ.get("APEX_REFERENCE_DIR", DEFAULT_REFERENCE_DIR))
+    ref = pathlib.Path(reference_dir or os.environ.get("APEX_REFERENCE_DIR") or SIBLING_REFERENCE_DIR)
     cpu_ref = ref / "src" / "tests" / "cpu_ref.h"
     doc = ref / "docs" / "B6_3_attention.md"
     if not (cpu_ref.exists() and doc.exists()):
