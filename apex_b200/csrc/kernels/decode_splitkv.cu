@@ -197,8 +197,9 @@ __device__ __forceinline__ void warp_step(const uint8_t *kbase, const uint8_t *v
     m_new[1] = fmaxf(m[1], my_g == 0 ? mo : mx);
 #pragma unroll
     for (int g = 0; g < kG; ++g) alpha[g] = fast_exp2(m[g] - m_new[g]);  // 0 when m = -inf
-    const float p = fast_exp2(s - m_new[my_g]);                          // 0 for invalid rows
-    lpart = lpart * alpha[my_g] + p;
+    // selects, not m_new[my_g] / alpha[my_g]: a lane-dependent index would put the arrays on the stack
+    const float p = fast_exp2(s - (my_g ? m_new[1] : m_new[0]));         // 0 for invalid rows
+    lpart = lpart * (my_g ? alpha[1] : alpha[0]) + p;
 #pragma unroll
     for (int g = 0; g < kG; ++g) {
 #pragma unroll
@@ -722,7 +723,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CL && ST > 1) ? 1 : 2)
             r[2] += wt * ov.z;
             r[3] += wt * ov.w;
         }
-        const float Mx = mx[g], dtot = dsum[g];
+        const float Mx = g ? mx[1] : mx[0], dtot = g ? dsum[1] : dsum[0];  // selects keep both in registers
         const float inv = dtot > 0.f ? 1.0f / dtot : 0.f;
         if (a.peer_mode) {
             const float on[4] = {r[0] * inv, r[1] * inv, r[2] * inv, r[3] * inv};

@@ -115,9 +115,10 @@ __global__ void __launch_bounds__(kThreads) nvfp4_matvec_kernel(const TIn *__res
     const uint32_t row0 = (blockIdx.x * kWarps + warp) * kRowsPerWarp;
     const uint32_t G = n / 16, wpr = n / 8;
     const bool fused = ep.weight != nullptr;
-    float sq[kFusedMaxTokens];
-#pragma unroll
-    for (int t = 0; t < static_cast<int>(kFusedMaxTokens); ++t) sq[t] = 0.f;
+    // per-token sums of squares of this warp's rows, kept by lane 0 in shared memory (a register
+    // array indexed by the runtime token would live on the stack)
+    if (lane == 0)
+        for (uint32_t t = 0; t < kFusedMaxTokens; ++t) s_sq[warp][t] = 0.f;
 
     for (uint32_t t0 = 0; t0 < tokens; t0 += kTok) {
         const uint32_t tc = min(static_cast<uint32_t>(kTok), tokens - t0);
@@ -182,8 +183,10 @@ __global__ void __launch_bounds__(kThreads) nvfp4_matvec_kernel(const TIn *__res
             for (int t = 0; t < kTok; ++t) {
                 const float v = warp_sum(acc[r][t]);
                 if (row < rows && t < static_cast<int>(tc)) {
-                    if (lane == 0) store(out + static_cast<uint64_t>(t0 + t) * rows + row, v);
-                    if (fused) sq[t0 + t] += v * v;  // t0 + t < kFusedMaxTokens when fused
+                    if (lane == 0) {
+                        store(out + static_cast<uint64_t>(t0 + t) * rows + row, v);
+                        if (fused) s_sq[warp][t0 + t] += v * v;  // t0 + t < kFusedMaxTokens when fused
+                    }
                 }
             }
         }
@@ -191,8 +194,6 @@ __global__ void __launch_bounds__(kThreads) nvfp4_matvec_kernel(const TIn *__res
     if (!fused) return;
 
     // ---- fused RMSNorm epilogue (tokens <= kFusedMaxTokens; TOut is float)
-    if (lane == 0)
-        for (uint32_t t = 0; t < tokens; ++t) s_sq[warp][t] = sq[t];
     __syncthreads();
     if (threadIdx.x < tokens) {
         float v = 0.f;
@@ -284,9 +285,9 @@ __global__ void __launch_bounds__(kThreads + 32, TK == 1 ? 2 : 1) nvfp4_stream_k
     }
 
     // ---------------------------------------------------------------------- consumers
-    float sq[kFusedMaxTokens];
-#pragma unroll
-    for (int t = 0; t < static_cast<int>(kFusedMaxTokens); ++t) sq[t] = 0.f;
+    // per-token sums of squares of this warp's rows, kept by lane 0 in shared memory
+    if (lane == 0)
+        for (uint32_t t = 0; t < kFusedMaxTokens; ++t) s_sq[warp][t] = 0.f;
     uint32_t k = 0;
     for (uint32_t tile = blockIdx.x; tile < ta.tiles; tile += gridDim.x, ++k) {
         const uint32_t slot = k % ta.stages;
@@ -338,9 +339,9 @@ __global__ void __launch_bounds__(kThreads + 32, TK == 1 ? 2 : 1) nvfp4_stream_k
 #pragma unroll
                 for (int t = 0; t < TK; ++t) {
                     const float v = warp_sum(acc[r][t]);
-                    if (row < ta.rows && t < static_cast<int>(tc)) {
-                        if (lane == 0) store(out + static_cast<uint64_t>(t0 + t) * ta.rows + row, v);
-                        if (fused) sq[t0 + t] += v * v;
+                    if (row < ta.rows && t < static_cast<int>(tc) && lane == 0) {
+                        store(out + static_cast<uint64_t>(t0 + t) * ta.rows + row, v);
+                        if (fused) s_sq[warp][t0 + t] += v * v;
                     }
                 }
             }
@@ -351,8 +352,6 @@ __global__ void __launch_bounds__(kThreads + 32, TK == 1 ? 2 : 1) nvfp4_stream_k
     if (!fused) return;
 
     // ---- fused RMSNorm epilogue (as in nvfp4_matvec_kernel), among the consumer warps
-    if (lane == 0)
-        for (uint32_t t = 0; t < ta.tokens; ++t) s_sq[warp][t] = sq[t];
     asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
     if (threadIdx.x < ta.tokens) {
         float v = 0.f;
