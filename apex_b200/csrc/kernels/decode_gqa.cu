@@ -39,6 +39,7 @@ constexpr int kStagePos = 16;      // keys per stage (MMA M)
 constexpr int kWarps = 4;          // consumer warps
 constexpr int kThreads = (kWarps + 1) * 32;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint32_t kMaxSplits = 4096;  // the last CTA's merge keeps kHeads x splits weights in the ring
 
 struct GqaArgs {
     const uint16_t *q_raw, *k_new, *v_new, *q_w, *k_w;
@@ -68,6 +69,9 @@ struct GqaSmem {
     uint64_t full[kStages], empty[kStages];
     int is_last;
 };
+static_assert(sizeof(GqaSmem<256>::ring) >= kHeads * kMaxSplits * sizeof(float) &&
+                  sizeof(GqaSmem<512>::ring) >= kHeads * kMaxSplits * sizeof(float),
+              "merge weights fit in the ring");
 
 __device__ __forceinline__ void gqa_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWarps * 32) : "memory"); }
 
@@ -435,27 +439,61 @@ __global__ void __launch_bounds__(kThreads, 1) decode_gqa_kernel(const __grid_co
     gqa_sync();
     if (!sm.is_last) return;
     __threadfence();
-    // ---- last CTA: merge the nsplit partials of every head (loads of all splits in flight)
-    for (uint32_t ch = tid; ch < G * (D / 4); ch += kWarps * 32) {
-        const uint32_t h = ch / (D / 4), d0 = (ch % (D / 4)) * 4;
+    // ---- last CTA: merge the nsplit partials of every head.  Warp w takes heads w, w + 4: the max
+    // of the splits' m, then their weights 2^(m - M) l into shared memory (the ring is free) and the
+    // weights' sum; then every thread accumulates its 4-dim chunks over the splits, eight
+    // independent 16-byte loads in flight.
+    float *wts = reinterpret_cast<float *>(sm.ring[0]);  // [G][nsplit]: G * nsplit * 4 <= 128 KB
+    float *den_h = sm.red_l[0];                          // [G] sums of the weights
+    for (uint32_t h = warp; h < G; h += kWarps) {
         const float *base = part + (rows_b + h) * a.max_splits * (D + 4);
         float M = -INFINITY;
-        for (uint32_t s = 0; s < nsplit; ++s) {
-            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(base + s * (D + 4) + D));
+        for (uint32_t sp = lane; sp < nsplit; sp += 32) {
+            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(base + sp * (D + 4) + D));
             if (ml.y > 0.f) M = fmaxf(M, ml.x);
         }
-        float den = 0.f, r4[4] = {0.f, 0.f, 0.f, 0.f};
-        for (uint32_t s = 0; s < nsplit; ++s) {
-            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(base + s * (D + 4) + D));
-            if (!(ml.y > 0.f)) continue;
-            const float wt = fast_exp2(ml.x - M) * ml.y;
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(base + s * (D + 4) + d0));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        float den = 0.f;
+        for (uint32_t sp = lane; sp < nsplit; sp += 32) {
+            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(base + sp * (D + 4) + D));
+            const float wt = ml.y > 0.f ? fast_exp2(ml.x - M) * ml.y : 0.f;
+            wts[h * nsplit + sp] = wt;
             den += wt;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+        if (lane == 0) den_h[h] = den;
+    }
+    gqa_sync();
+    for (uint32_t ch = tid; ch < G * (D / 4); ch += kWarps * 32) {
+        const uint32_t h = ch / (D / 4), d0 = (ch % (D / 4)) * 4;
+        const float *pg = part + (rows_b + h) * a.max_splits * (D + 4) + d0;
+        const float *wg = wts + h * nsplit;
+        float r4[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t sp = 0;
+        for (; sp + 8 <= nsplit; sp += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = __ldcg(reinterpret_cast<const float4 *>(pg + (sp + u) * (D + 4)));
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float wt = wg[sp + u];
+                r4[0] += wt * v[u].x;
+                r4[1] += wt * v[u].y;
+                r4[2] += wt * v[u].z;
+                r4[3] += wt * v[u].w;
+            }
+        }
+        for (; sp < nsplit; ++sp) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(pg + sp * (D + 4)));
+            const float wt = wg[sp];
             r4[0] += wt * v.x;
             r4[1] += wt * v.y;
             r4[2] += wt * v.z;
             r4[3] += wt * v.w;
         }
+        const float den = den_h[h];
         const float inv = den > 0.f ? 1.0f / den : 0.f;
         uint2 pk;
         pk.x = pack_bf16(r4[0] * inv, r4[1] * inv);
@@ -467,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_gqa_kernel(const __grid_co
 uint32_t gqa_max_splits(uint32_t batch, uint32_t kv_heads, uint32_t max_len) {
     const uint64_t by_len = (static_cast<uint64_t>(max_len) + 63) / 64;
     const uint64_t by_grid = static_cast<uint64_t>(sm_count()) * 4 / std::max<uint64_t>(1, uint64_t(batch) * kv_heads) + 2;
-    return static_cast<uint32_t>(std::max<uint64_t>(1, std::min({by_len, by_grid, uint64_t(4096)})));
+    return static_cast<uint32_t>(std::max<uint64_t>(1, std::min({by_len, by_grid, uint64_t(kMaxSplits)})));
 }
 
 // Keys per split: whole waves of CTAs (one per SM) with every (sequence, kv head) cut into the same

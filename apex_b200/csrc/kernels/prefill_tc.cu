@@ -14,9 +14,10 @@
 //     3-D TMA box per 128-query tile), k and v to the caches.  It also zeroes the attention
 //     kernel's scheduler counters.
 //  2. attention: a persistent kernel of CTA pairs (clusters of two on two SMs).  A pair takes
-//     work items from an atomic counter, heaviest first: 256 query rows = the same 128 queries
-//     for the two q heads of a GQA group (head 2i+r in CTA r) when the group size is even,
-//     else 256 consecutive queries of one head (rows 128r.. in CTA r).  Both products are
+//     its first work item by its cluster index and later ones from an atomic counter, heaviest
+//     first: 256 query rows = the same 128 queries for the two q heads of a GQA group (head
+//     2i+r in CTA r) when the group size is even, else 256 consecutive queries of one head (rows
+//     128r.. in CTA r).  Both products are
 //     M=256 tcgen05.mma.cta_group::2.kind::f16 issued by one thread of CTA 0:
 //       S_t = Q K_t^T  (N=128 keys, K=256): Q (128 rows x 256, this CTA's) and this CTA's half
 //                      of the key tile (64 keys x 256) in shared memory, K-major;
@@ -209,6 +210,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const bool leader = rank == 0;
 
     if (tid == 0) {
+        // the descriptors' first fetch takes about a microsecond: start it before the set-up
+        prefetch_tensormap(&tm_q);
+        prefetch_tensormap(&tm_k);
+        prefetch_tensormap(&tm_v);
+        prefetch_tensormap(&tm_o);
         mbar_init(bar(kBarQFull), 1);
         mbar_init(bar(kBarQEmpty), 1);
         for (int i = 0; i < kSlots; ++i) {
@@ -245,9 +251,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         reg_dealloc<kRegsTmaMma>();
         if (warp == 0 && lane == 0) {
             // -------------------------------------------------------- TMA producer (+ scheduler in CTA 0)
-            prefetch_tensormap(&tm_q);
-            prefetch_tensormap(&tm_k);
-            prefetch_tensormap(&tm_v);
             // Everything above overlapped the preceding kernel (the prep); from here on this
             // thread reads its outputs (scheduler counters, q, K, V), and every other role only
             // acts on items and data this thread hands on.
@@ -285,7 +288,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const uint32_t is = it % kItemRing;
                 int idx;
                 if (leader) {
-                    const uint32_t claimed = atomicAdd(a.sched, 1u);
+                    // each pair's first item is its cluster index (no round trip to a counter that
+                    // every pair hits at once); later items come from the counter, past those
+                    const uint32_t pairs = gridDim.x / 2;
+                    const uint32_t claimed = it == 0 ? blockIdx.x / 2 : pairs + atomicAdd(a.sched, 1u);
                     idx = claimed < a.n_items ? static_cast<int>(claimed) : -1;
                     items[is] = idx;
                     st_cluster_u32(mapa(sb + kOffItems + 4 * is, 1), static_cast<uint32_t>(idx));
