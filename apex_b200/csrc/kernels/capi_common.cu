@@ -129,8 +129,8 @@ int make_tensor_map_bf16_3d_box(CUtensorMap *map, const void *base, const uint64
     return APEX_OK;
 }
 
-int make_tensor_map_bf16_4d_sw64(CUtensorMap *map, const void *base, const uint64_t (&dims)[4],
-                                 const uint64_t (&strides_bytes)[3], const uint32_t (&box)[4]) {
+int make_tensor_map_bf16_4d(CUtensorMap *map, const void *base, const uint64_t (&dims)[4],
+                            const uint64_t (&strides_bytes)[3], const uint32_t (&box)[4], bool swizzle128) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return fail(APEX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     const cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
@@ -138,7 +138,8 @@ int make_tensor_map_bf16_4d_sw64(CUtensorMap *map, const void *base, const uint6
     const cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
     const cuuint32_t estride[4] = {1, 1, 1, 1};
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), d, st, bx, estride,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                          CU_TENSOR_MAP_L2_PROMOTION_NONE,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail(APEX_ERR_INVALID_ARGUMENT,

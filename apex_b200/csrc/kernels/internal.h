@@ -34,11 +34,11 @@ int make_tensor_map_bf16_3d(CUtensorMap *map, const void *base, uint64_t d0, uin
 int make_tensor_map_bf16_3d_box(CUtensorMap *map, const void *base, const uint64_t (&dims)[3],
                                 const uint64_t (&strides_bytes)[2], const uint32_t (&box)[3]);
 
-// A 4-D bf16 tensor map with 64-byte swizzle, for tiled stores of 32-element (64-byte) rows:
-// dims {d0 (innermost), d1, d2, d3}, byte strides of dims 1..3, box {box0, box1, box2, box3}.
-// Elements outside the tensor are not written.
-int make_tensor_map_bf16_4d_sw64(CUtensorMap *map, const void *base, const uint64_t (&dims)[4],
-                                 const uint64_t (&strides_bytes)[3], const uint32_t (&box)[4]);
+// A 4-D bf16 tensor map for tiled stores, 128-byte swizzle (rows of up to 64 elements) or 64-byte
+// swizzle (up to 32): dims {d0 (innermost), d1, d2, d3}, byte strides of dims 1..3, box {box0, box1,
+// box2, box3}.  Elements outside the tensor are not written.
+int make_tensor_map_bf16_4d(CUtensorMap *map, const void *base, const uint64_t (&dims)[4],
+                            const uint64_t (&strides_bytes)[3], const uint32_t (&box)[4], bool swizzle128);
 
 // inv_freq[i] = base^(-2i/head_dim) (f32 exponent, double-precision power rounded to f32) for
 // i < pairs, the frequencies of shaders/head_norm_rope.metal:59.

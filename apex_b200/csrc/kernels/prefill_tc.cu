@@ -52,20 +52,24 @@ namespace {
 constexpr int kD = 256;
 constexpr int kBM = 128;                             // query rows per CTA
 constexpr int kBN = 128;                             // keys per tile (both CTAs)
-constexpr int kSlots = 9;
+constexpr int kSlots = 10;
 constexpr uint32_t kChunk = 64 * 128;                // 64 rows x 128 B (one TMA box)
 constexpr uint32_t kSlotBytes = 2 * kChunk;          // 16 KB
 constexpr uint32_t kQBytes = kBM * kD * 2;           // 64 KB
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffSlots = kQBytes;
-constexpr uint32_t kOffStage = kOffSlots + kSlots * kSlotBytes;  // epilogue staging: 4 warps x 2 x [32 rows][64 B]
-constexpr uint32_t kStageBytes = 32 * 64;
-constexpr uint32_t kStageWarpBytes = 2 * kStageBytes;
-constexpr uint32_t kOffBar = kOffStage + 4 * kStageWarpBytes;
+// The epilogue stages each item's output in four ring slots (one per epilogue warp: its 32 rows
+// as four [32 rows][128 B] tiles, 128-byte swizzle), taken in ring order right after the item's
+// last V tile and handed back once the output stores have read them.
+constexpr uint32_t kBoxBytes = 32 * 128;             // one output store: 32 rows x 64 dims
+constexpr uint32_t kStageSlots = 4;                  // ring slots per item's output
+static_assert(kSlotBytes == 4 * kBoxBytes, "one epilogue warp's 32 rows fill one slot");
+constexpr uint32_t kOffBar = kOffSlots + kSlots * kSlotBytes;
 constexpr uint32_t kNumBars = 48;
 constexpr uint32_t kOffItems = kOffBar + 8 * kNumBars;
 constexpr uint32_t kItemRing = 8;
-constexpr uint32_t kOffRed = kOffItems + 4 * kItemRing;  // row sums, float [2 item parity][2 half][128]
+constexpr uint32_t kOffStageSlot = kOffItems + 4 * kItemRing;  // uint32 [2 item parity][4 warps]
+constexpr uint32_t kOffRed = kOffStageSlot + 4 * 2 * kStageSlots;  // row sums, float [2 item parity][2 half][128]
 constexpr uint32_t kOffFlag = kOffRed + 2 * 2 * 128 * 4;
 constexpr uint32_t kOffTmem = kOffFlag + 16;
 constexpr uint32_t kSmemBytes = kOffTmem + 16;  // the dynamic shared memory base is 1024-aligned
@@ -84,19 +88,21 @@ constexpr uint32_t kRegsTmaMma = 64, kRegsSoftmax = 168, kRegsEpilogue = 112;
 static_assert(kRegsTmaMma + 2 * kRegsSoftmax + kRegsEpilogue == 4 * (65536 / kThreads), "register split");
 
 static_assert(kSmemBytes <= 232448, "shared memory budget");
-static_assert(kOffStage % 1024 == 0, "64-byte-swizzled staging tiles need 512-byte alignment");
+static_assert(kOffSlots % 1024 == 0 && kSlotBytes % 1024 == 0, "swizzled tiles need 1024-byte slots");
 
 // barrier indices (8 bytes each at kOffBar).  CTA 0's copies of QFull, Full, P and OFree count
 // the pair; Empty, QEmpty, S and O are signalled in both CTAs by multicast commits.  P is one
 // barrier per (softmax half, tile parity), so PV can start on the first 64 keys early.  L (row
 // sums written, by item parity) and LFree (row sums read) pass the row sums from the softmax
 // warps to the epilogue warps of the same CTA.  OItem completes once per item, when its last PV
-// is done: the epilogue waits on it rather than on O, whose phase may lag two behind.
+// is done: the epilogue waits on it rather than on O, whose phase may lag two behind.  Stage (by
+// item parity, each CTA its own) tells the epilogue warps that the producer has taken the item's
+// four staging slots; they hand each slot back on the slot's Empty barrier of their own CTA.
 constexpr int kBarQFull = 0, kBarQEmpty = 1, kBarFull = 2, kBarEmpty = kBarFull + kSlots,
               kBarS = kBarEmpty + kSlots, kBarP = kBarS + 2, kBarO = kBarP + 4, kBarOFree = kBarO + 2,
               kBarItem = kBarOFree + 1, kBarL = kBarItem + kItemRing, kBarLFree = kBarL + 2,
-              kBarOItem = kBarLFree + 2;
-static_assert(kBarOItem + 1 <= kNumBars, "barrier budget");
+              kBarOItem = kBarLFree + 2, kBarStage = kBarOItem + 1;
+static_assert(kBarStage + 2 <= kNumBars, "barrier budget");
 
 struct PrefillArgs {
     uint16_t *out;        // [B][T][Hq][D]
@@ -230,6 +236,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         mbar_init(bar(kBarOFree), kEpiPairWarps);
         mbar_init(bar(kBarOItem), 1);
+        for (int i = 0; i < 2; ++i) mbar_init(bar(kBarStage + i), 1);
         for (uint32_t i = 0; i < kItemRing; ++i) mbar_init(bar(kBarItem + i), 1);
         *err_flag = 0;
         fence_mbar_init();
@@ -284,6 +291,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
                 pend = false;
             };
+            // the next four ring positions become item `item`'s output staging: each waits for its
+            // slot like a load, completes its Full phase with no bytes (CTA 0), and goes to the
+            // epilogue warp of its index; the MMA issuer passes over the same four positions
+            uint32_t *stage_slot = reinterpret_cast<uint32_t *>(base + kOffStageSlot);
+            auto reserve_stage = [&](uint32_t item) {
+                for (uint32_t q = 0; q < kStageSlots; ++q) {
+                    const uint32_t slot = n % kSlots;
+                    if (n >= kSlots && !mbar_wait(bar(kBarEmpty + slot), ((n / kSlots) - 1) & 1, a.status)) {
+                        alive = false;
+                        return;
+                    }
+                    if (leader) mbar_arrive(bar(kBarFull + slot));
+                    stage_slot[(item & 1) * kStageSlots + q] = slot;
+                    ++n;
+                }
+                mbar_arrive(bar(kBarStage + (item & 1)));
+            };
+            uint32_t taken = 0;  // items this pair took
             for (uint32_t it = 0; alive; ++it) {
                 const uint32_t is = it % kItemRing;
                 int idx;
@@ -305,6 +330,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     idx = items[is];
                 }
                 if (idx < 0) break;
+                taken = it + 1;
                 const Item g = item_geometry(static_cast<uint32_t>(idx), a, rank);
                 const int32_t kv_row = static_cast<int32_t>(g.b * a.kv_heads + g.kvh);
                 for (uint32_t j = 0; j < g.n_tiles && alive; ++j) {
@@ -331,13 +357,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             tma_load_3d_pair(sb + kOffQ + c * (kQBytes / 4), &tm_q, 64 * c,
                                              static_cast<int32_t>(g.q_row),
                                              static_cast<int32_t>(g.b * a.q_heads + g.h), full);
+                        if (it >= 1) reserve_stage(it - 1);  // the previous item's last V is in the ring
                     }
                     pend = true;
                     pend_key = g.j_start + j * kBN;
                     pend_row = kv_row;
                 }
             }
-            if (pend && alive) load_v();
+            if (pend && alive) {
+                load_v();
+                if (alive) reserve_stage(taken - 1);
+            }
         } else if (warp == 1 && leader) {
             // -------------------------------------------------------- MMA issuer (CTA 0)
             // The whole warp runs the loop (its values stay warp-uniform) and one elected lane issues
@@ -378,7 +408,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     ++n;
                 }
                 tc_commit_pair_both(bar(kBarO + (t & 1)));
-                if (last) tc_commit_pair_both(bar(kBarOItem));
+                if (last) {
+                    tc_commit_pair_both(bar(kBarOItem));
+                    // the item's four output-staging positions: no MMA reads them
+                    for (uint32_t q = 0; q < kStageSlots && alive; ++q) {
+                        alive = wait_full(n);
+                        ++n;
+                    }
+                }
             };
             bool pend = false, pend_first = false, pend_last = false;  // PV of the previous tile, issued after the next S
             uint32_t pend_t = 0, pend_it = 0;
@@ -576,16 +613,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------------------------ epilogue (both CTAs)
         // O / l -> bf16 out[b][t][h][...] for this CTA's 128 rows, once the item's last PV is done.
-        // Each 32-column chunk of a warp's 32 rows goes to global memory as one TMA store from a
-        // 2 KB staging tile ([32 rows][64 B], 64-byte swizzle: 16-byte piece q of row x at
-        // ((q ^ ((x >> 1) & 3)) * 16)), two tiles per warp in turn; rows at or past T are clipped by
-        // the tensor map.  O is released to the next item's PV once the last chunk is in registers.
+        // Warp q stages its 32 rows in the ring slot the producer took for it (four [32 rows][128 B]
+        // tiles, 128-byte swizzle: 16-byte piece c of row x at ((c ^ (x & 7)) * 16)), so the
+        // four 64-column rounds never wait for a store to read a tile: O goes back to the next
+        // item's PV as soon as its last columns are in registers.  Then one TMA store per tile (rows
+        // at or past T clipped by the tensor map) and, once they have read the slot, the slot goes
+        // back to the producer on its Empty barrier.
         reg_dealloc<kRegsEpilogue>();
         const uint32_t quad = warp & 3;
         const uint32_t r = quad * 32 + lane;
         const uint32_t lane_base = tmem + ((32u * quad) << 16);
         const uint32_t ofree_bar = mapa(bar(kBarOFree), 0);
-        uint8_t *stg = base + kOffStage + quad * kStageWarpBytes;
+        const uint32_t *stage_slot = reinterpret_cast<const uint32_t *>(base + kOffStageSlot);
         for (uint32_t it = 0; alive; ++it) {
             if (!__all_sync(0xffffffffu, mbar_wait_cluster(bar(kBarItem + it % kItemRing), (it / kItemRing) & 1,
                                                             a.status))) {
@@ -596,9 +635,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (idx < 0) break;
             const Item g = item_geometry(static_cast<uint32_t>(idx), a, rank);
             // the item's last PV (OItem completes once per item; the next item's PVs wait for this
-            // warp's O release, so the barrier cannot run a phase ahead)
+            // warp's O release, so the barrier cannot run a phase ahead), its row sums, its slots
             if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarOItem), it & 1, a.status)) ||
-                !__all_sync(0xffffffffu, mbar_wait(bar(kBarL + (it & 1)), (it >> 1) & 1, a.status))) {
+                !__all_sync(0xffffffffu, mbar_wait(bar(kBarL + (it & 1)), (it >> 1) & 1, a.status)) ||
+                !__all_sync(0xffffffffu, mbar_wait(bar(kBarStage + (it & 1)), (it >> 1) & 1, a.status))) {
                 alive = false;
                 break;
             }
@@ -607,8 +647,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_arrive(bar(kBarLFree + (it & 1)));
             const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
             const bool any_rows = quad * 32 < g.rows_valid;
-            // 64 columns per TMEM load; each pair of 32-column chunks is packed to bf16 as soon as it
-            // lands, the next load is issued before the pair is staged, so a load is always in flight
+            const uint32_t slot = stage_slot[(it & 1) * kStageSlots + quad];
+            const uint32_t stg = sb + kOffSlots + slot * kSlotBytes;  // 1024-aligned
+            const uint32_t row_base = stg + lane * 128 + ((lane & 7) << 4);
+            // 64 columns per TMEM load; each is packed to bf16 and staged while the next is in flight
             uint32_t raw[64];
             uint32_t(&raw_lo)[32] = *reinterpret_cast<uint32_t(*)[32]>(&raw[0]);
             uint32_t(&raw_hi)[32] = *reinterpret_cast<uint32_t(*)[32]>(&raw[32]);
@@ -620,33 +662,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 32; ++i) pk[i] = scale_pack_bf16(raw[2 * i], raw[2 * i + 1], inv_l);
                 if (pr < 3) tmem_ld64(lane_base + kColO + 64 * (pr + 1), raw);
-                if (lane == 0) bulk_wait_read_all();  // the previous pair's stores have read both tiles
-                __syncwarp();
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    uint8_t *buf = stg + h * kStageBytes;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        *reinterpret_cast<uint4 *>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) =
-                            make_uint4(pk[16 * h + 4 * q], pk[16 * h + 4 * q + 1], pk[16 * h + 4 * q + 2],
-                                       pk[16 * h + 4 * q + 3]);
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0 && any_rows) {
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
-                        tma_store_4d(&tm_o, smem_u32(stg + h * kStageBytes), static_cast<int32_t>(64 * pr + 32 * h),
-                                     static_cast<int32_t>(g.h), static_cast<int32_t>(g.t0 + quad * 32),
-                                     static_cast<int32_t>(g.b));
-                    bulk_commit_group();
-                }
+                for (int c = 0; c < 8; ++c)  // piece c of row `lane` at (c ^ (lane & 7)) * 16
+                    st_shared_v4((row_base ^ (c << 4)) + pr * kBoxBytes,
+                                 make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]));
                 if (pr < 3) tc_wait_ld(raw_lo, raw_hi);
                 if (pr == 2) {  // all of O is in registers: the next item's first PV may overwrite it
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive_remote(ofree_bar);
                 }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                if (any_rows) {
+#pragma unroll
+                    for (int b4 = 0; b4 < 4; ++b4)
+                        tma_store_4d(&tm_o, stg + b4 * kBoxBytes, static_cast<int32_t>(64 * b4), static_cast<int32_t>(g.h),
+                                     static_cast<int32_t>(g.t0 + quad * 32), static_cast<int32_t>(g.b));
+                    bulk_commit_group();
+                    bulk_wait_read_all();  // the stores have read the slot
+                }
+                mbar_arrive(bar(kBarEmpty + slot));
             }
         }
         if (lane == 0) bulk_wait_all();
@@ -968,11 +1006,11 @@ int launch_attend(const apex_attn_params *p, void *workspace, const uint16_t *k_
     rc = make_tensor_map_bf16_3d(&tv, v_cache, kD, kv_len, kv_rows, kD * 2ull, static_cast<uint64_t>(capacity) * kD * 2,
                                  64, 64);
     if (rc) return rc;
-    // output [B][T][Hq][256] as {256, Hq, T, B}: one box = 32 dims x 1 head x 32 queries
+    // output [B][T][Hq][256] as {256, Hq, T, B}: one box = 64 dims x 1 head x 32 queries
     CUtensorMap to;
     const uint64_t row = static_cast<uint64_t>(kD) * 2;
-    rc = make_tensor_map_bf16_4d_sw64(&to, out, {static_cast<uint64_t>(kD), p->q_heads, tokens, batch},
-                                      {row, row * p->q_heads, row * p->q_heads * tokens}, {32, 1, 32, 1});
+    rc = make_tensor_map_bf16_4d(&to, out, {static_cast<uint64_t>(kD), p->q_heads, tokens, batch},
+                                 {row, row * p->q_heads, row * p->q_heads * tokens}, {64, 1, 32, 1}, true);
     if (rc) return rc;
     static bool attr_set[64] = {};
     int dev = 0;
