@@ -69,7 +69,7 @@ TOL_SPLIT_MAX, TOL_SPLIT_MEAN = 4e-3, 2e-4  # KV split vs the one-GPU decode (sa
 # K/V streaming and grows in proportion.
 _C5_B1_TRAFFIC = 1_073_923_000 + 6_035_712
 NCU_TRAFFIC_BYTES = {
-    "c2_prefill_window": 33_634_560 + 143_872,
+    "c2_prefill_window": 33_638_400 + 13_312,
     "c3_ragged_decode": 2_307_200_000,
     "c5_long_decode_b1": _C5_B1_TRAFFIC,
     "c5_long_decode_b8": 8 * _C5_B1_TRAFFIC,
