@@ -31,7 +31,7 @@ EXPORTED = (
     "apex_attn_prefill_prep_bf16", "apex_attn_prefill_attend_bf16", "apex_attn_decode_bf16_noalloc",
     "apex_attn_peer_exchange_bytes", "apex_attn_decode_kvsplit_bf16", "apex_device_alloc",
     "apex_device_free", "apex_ipc_get_handle", "apex_ipc_open_handle", "apex_ipc_close_handle",
-    "apex_kv_ring_store", "apex_matmul_nvfp4_f32", "apex_matmul_nvfp4", "apex_rms_norm_f32", "apex_matmul_nvfp4_rms_norm_workspace_bytes",
+    "apex_kv_ring_store", "apex_matmul_nvfp4_f32", "apex_matmul_nvfp4", "apex_matmul_nvfp4_multi", "apex_rms_norm_f32", "apex_matmul_nvfp4_rms_norm_workspace_bytes",
     "apex_matmul_nvfp4_rms_norm",
     # include/apex_loader.h
     "apex_model_open", "apex_model_close", "apex_model_summary_get", "apex_model_tensor", "apex_model_expert_piece",
@@ -122,6 +122,7 @@ def load(path: str | pathlib.Path | None = None):
     L.apex_kv_ring_store.argtypes = [_vp] * 4 + [_u32] * 6 + [_vp]
     L.apex_matmul_nvfp4_f32.argtypes = [_vp] * 4 + [_u32] * 3 + [_vp]
     L.apex_matmul_nvfp4.argtypes = [_vp, _i32, _vp, _vp, _vp, _i32, _u32, _u32, _u32, _vp]
+    L.apex_matmul_nvfp4_multi.argtypes = [_vp, _i32, _u32, _vp, _vp, _vp, _vp, _i32, _u32, _u32, _vp]
     L.apex_rms_norm_f32.argtypes = [_vp, _vp, _vp, _u32, _u32, _f32, _vp]
     L.apex_matmul_nvfp4_rms_norm_workspace_bytes.argtypes = [_u32, _u32]
     L.apex_matmul_nvfp4_rms_norm_workspace_bytes.restype = _sz

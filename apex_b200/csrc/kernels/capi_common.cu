@@ -154,7 +154,7 @@ extern "C" {
 
 const char *apex_cuda_last_error(void) { return apex::t_last_error.c_str(); }
 
-int apex_cuda_abi_version(void) { return 102; }
+int apex_cuda_abi_version(void) { return 103; }
 
 int apex_cuda_device_status(void *stream) {
     unsigned int host = 0;

@@ -236,17 +236,35 @@ constexpr int kMaxStages = 4;
 constexpr uint32_t kStageBudget = 200u * 1024u;
 
 struct TileArgs {
-    uint32_t tokens, rows, n, tiles, stages;
+    uint32_t tokens, n, tiles, stages;  // tiles: of all matrices
     uint32_t code_bytes, scale_bytes, stage_bytes;  // per tile / per stage
     unsigned *status;
 };
 
+// Up to four matrices of the same width over the same input (q, k and v of one layer): one launch
+// walks the tiles of all of them, matrix m owning tiles [tile0[m], tile0[m + 1]).
+constexpr int kMaxMats = 4;
+struct StreamMats {
+    const uint32_t *codes[kMaxMats];
+    const uint8_t *scales[kMaxMats];
+    void *out[kMaxMats];
+    uint32_t rows[kMaxMats];
+    uint32_t tile0[kMaxMats + 1];
+    uint32_t count;
+};
+
+__device__ __forceinline__ uint32_t mat_of(const StreamMats &m, uint32_t tile) {
+    uint32_t i = 0;
+#pragma unroll
+    for (int j = 1; j < kMaxMats; ++j)
+        if (static_cast<uint32_t>(j) < m.count && tile >= m.tile0[j]) i = j;
+    return i;
+}
+
 template <typename TIn, typename TOut, int TK>
 __global__ void __launch_bounds__(kThreads + 32, TK == 1 ? 2 : 1) nvfp4_stream_kernel(const TIn *__restrict__ input,
-                                                                        const uint32_t *__restrict__ codes,
-                                                                        const uint8_t *__restrict__ scales,
-                                                                        TOut *__restrict__ out, const TileArgs ta,
-                                                                        NormEpilogue ep) {
+                                                                        const __grid_constant__ StreamMats mats,
+                                                                        const TileArgs ta, NormEpilogue ep) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[kMaxStages], empty[kMaxStages];
     __shared__ float s_sq[kWarps][kFusedMaxTokens];
@@ -270,15 +288,18 @@ __global__ void __launch_bounds__(kThreads + 32, TK == 1 ? 2 : 1) nvfp4_stream_k
             for (uint32_t tile = blockIdx.x; tile < ta.tiles; tile += gridDim.x, ++k) {
                 const uint32_t slot = k % ta.stages;
                 if (k >= ta.stages && !mbar_wait(smem_u32(&empty[slot]), ((k / ta.stages) - 1) & 1, ta.status)) break;
-                const uint32_t nrows = min(static_cast<uint32_t>(kTileRows), ta.rows - tile * kTileRows);
+                const uint32_t m = mat_of(mats, tile), local = tile - mats.tile0[m];
+                const uint32_t nrows = min(static_cast<uint32_t>(kTileRows), mats.rows[m] - local * kTileRows);
                 const uint32_t cb = nrows * (n / 2), sb = nrows * G;
                 uint8_t *st = smem + static_cast<size_t>(slot) * ta.stage_bytes;
                 const uint32_t fb = smem_u32(&full[slot]);
                 // both runs are multiples of 16 bytes at 16-byte offsets (the host checks n and rows)
                 mbar_arrive_expect_tx(fb, cb + sb);
-                tma_bulk_load(smem_u32(st), reinterpret_cast<const uint8_t *>(codes) + static_cast<uint64_t>(tile) * ta.code_bytes,
+                tma_bulk_load(smem_u32(st),
+                              reinterpret_cast<const uint8_t *>(mats.codes[m]) + static_cast<uint64_t>(local) * ta.code_bytes,
                               cb, fb);
-                tma_bulk_load(smem_u32(st + ta.code_bytes), scales + static_cast<uint64_t>(tile) * ta.scale_bytes, sb, fb);
+                tma_bulk_load(smem_u32(st + ta.code_bytes), mats.scales[m] + static_cast<uint64_t>(local) * ta.scale_bytes,
+                              sb, fb);
             }
         }
         return;
@@ -293,7 +314,10 @@ __global__ void __launch_bounds__(kThreads + 32, TK == 1 ? 2 : 1) nvfp4_stream_k
         const uint32_t slot = k % ta.stages;
         if (!mbar_wait(smem_u32(&full[slot]), (k / ta.stages) & 1, ta.status)) break;
         const uint8_t *st = smem + static_cast<size_t>(slot) * ta.stage_bytes;
-        const uint32_t rbase = tile * kTileRows;
+        const uint32_t m = mat_of(mats, tile);
+        const uint32_t rows = mats.rows[m];
+        TOut *out = static_cast<TOut *>(mats.out[m]);
+        const uint32_t rbase = (tile - mats.tile0[m]) * kTileRows;
         const uint32_t lr0 = warp * kRowsPerWarp;  // rows lr0, lr0+1 of the tile
         for (uint32_t t0 = 0; t0 < ta.tokens; t0 += TK) {
             const uint32_t tc = min(static_cast<uint32_t>(TK), ta.tokens - t0);
@@ -316,7 +340,7 @@ __global__ void __launch_bounds__(kThreads + 32, TK == 1 ? 2 : 1) nvfp4_stream_k
 #pragma unroll
                 for (int r = 0; r < kRowsPerWarp; ++r) {
                     const uint32_t lr = lr0 + r;
-                    if (rbase + lr >= ta.rows) break;
+                    if (rbase + lr >= rows) break;
                     const uint2 cw = *reinterpret_cast<const uint2 *>(st + static_cast<size_t>(lr) * (n / 2) + 8u * g);
                     const float s = e4m3_to_f32(st[ta.code_bytes + static_cast<size_t>(lr) * G + g]);
                     float w[16];
@@ -339,8 +363,8 @@ __global__ void __launch_bounds__(kThreads + 32, TK == 1 ? 2 : 1) nvfp4_stream_k
 #pragma unroll
                 for (int t = 0; t < TK; ++t) {
                     const float v = warp_sum(acc[r][t]);
-                    if (row < ta.rows && t < static_cast<int>(tc) && lane == 0) {
-                        store(out + static_cast<uint64_t>(t0 + t) * ta.rows + row, v);
+                    if (row < rows && t < static_cast<int>(tc) && lane == 0) {
+                        store(out + static_cast<uint64_t>(t0 + t) * rows + row, v);
                         if (fused) s_sq[warp][t0 + t] += v * v;
                     }
                 }
@@ -372,12 +396,14 @@ __global__ void __launch_bounds__(kThreads + 32, TK == 1 ? 2 : 1) nvfp4_stream_k
     if (threadIdx.x < ta.tokens) {
         float total = 0.f;
         for (uint32_t c = 0; c < gridDim.x; ++c) total += __ldcg(ep.ws_sumsq + static_cast<uint64_t>(c) * ta.tokens + threadIdx.x);
-        s_inv[threadIdx.x] = rsqrtf(total / static_cast<float>(ta.rows) + ep.eps);
+        s_inv[threadIdx.x] = rsqrtf(total / static_cast<float>(mats.rows[0]) + ep.eps);
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
-    float *o = reinterpret_cast<float *>(out);
-    for (uint64_t i = threadIdx.x; i < static_cast<uint64_t>(ta.tokens) * ta.rows; i += kThreads) {
-        const uint32_t t = static_cast<uint32_t>(i / ta.rows), r = static_cast<uint32_t>(i % ta.rows);
+    // the fused norm runs with one matrix (the host checks)
+    const uint32_t rows0 = mats.rows[0];
+    float *o = static_cast<float *>(mats.out[0]);
+    for (uint64_t i = threadIdx.x; i < static_cast<uint64_t>(ta.tokens) * rows0; i += kThreads) {
+        const uint32_t t = static_cast<uint32_t>(i / rows0), r = static_cast<uint32_t>(i % rows0);
         const float y = __ldcg(o + i) * s_inv[t] * __uint_as_float(static_cast<uint32_t>(ep.weight[r]) << 16);
         o[i] = y;
         if (ep.residual_out) ep.residual_out[i] = (ep.residual ? ep.residual[i] : 0.f) + y;
@@ -431,15 +457,15 @@ int check_matvec(const void *input, const uint32_t *codes, const uint8_t *scales
 
 // The streaming form applies when every tile's codes and scales are whole 16-byte runs at 16-byte
 // offsets (n a multiple of 32, and of 256 unless the rows fill whole tiles) and two stages fit.
-bool stream_plan(const uint32_t *codes, const uint8_t *scales, uint32_t n, uint32_t rows, uint32_t tokens,
-                 TileArgs &ta, uint32_t &grid, size_t &smem) {
-    if (n % 32 || (n % 256 && rows % kTileRows) || (reinterpret_cast<uintptr_t>(codes) & 15) ||
-        (reinterpret_cast<uintptr_t>(scales) & 15))
-        return false;
+bool stream_plan(const StreamMats &mats, uint32_t n, uint32_t tokens, TileArgs &ta, uint32_t &grid, size_t &smem) {
+    if (n % 32) return false;
+    for (uint32_t m = 0; m < mats.count; ++m)
+        if ((n % 256 && mats.rows[m] % kTileRows) || (reinterpret_cast<uintptr_t>(mats.codes[m]) & 15) ||
+            (reinterpret_cast<uintptr_t>(mats.scales[m]) & 15))
+            return false;
     ta.tokens = tokens;
-    ta.rows = rows;
     ta.n = n;
-    ta.tiles = (rows + kTileRows - 1) / kTileRows;
+    ta.tiles = mats.tile0[mats.count];
     ta.code_bytes = kTileRows * (n / 2);
     ta.scale_bytes = kTileRows * (n / 16);
     ta.stage_bytes = (ta.code_bytes + ta.scale_bytes + 127) & ~127u;
@@ -453,23 +479,40 @@ bool stream_plan(const uint32_t *codes, const uint8_t *scales, uint32_t n, uint3
     return ta.status != nullptr;
 }
 
+StreamMats one_matrix(const uint32_t *codes, const uint8_t *scales, void *output, uint32_t rows) {
+    StreamMats m{};
+    m.codes[0] = codes;
+    m.scales[0] = scales;
+    m.out[0] = output;
+    m.rows[0] = rows;
+    m.tile0[1] = (rows + kTileRows - 1) / kTileRows;
+    m.count = 1;
+    return m;
+}
+
+template <typename TIn, typename TOut>
+int launch_stream(const void *input, const StreamMats &mats, const TileArgs &ta, uint32_t grid, size_t smem,
+                  const NormEpilogue &ep, void *stream, const char *name) {
+    auto *kernel = ta.tokens == 1 ? nvfp4_stream_kernel<TIn, TOut, 1> : nvfp4_stream_kernel<TIn, TOut, kTok>;
+    int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kStageBudget)),
+                        name);
+    if (rc) return rc;
+    kernel<<<grid, kThreads + 32, smem, static_cast<cudaStream_t>(stream)>>>(static_cast<const TIn *>(input), mats,
+                                                                             ta, ep);
+    rc = check_cuda(cudaGetLastError(), name);
+    return rc ? rc : ok();
+}
+
 template <typename TIn, typename TOut>
 int launch_matvec(const void *input, const uint32_t *codes, const uint8_t *scales, void *output, uint32_t n,
                   uint32_t rows, uint32_t tokens, const NormEpilogue &ep, void *stream, const char *name) {
     TileArgs ta{};
     uint32_t grid = 0;
     size_t smem = 0;
-    if (stream_plan(codes, scales, n, rows, tokens, ta, grid, smem)) {
-        auto *kernel = tokens == 1 ? nvfp4_stream_kernel<TIn, TOut, 1> : nvfp4_stream_kernel<TIn, TOut, kTok>;
-        int rc = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 static_cast<int>(kStageBudget)),
-                            name);
-        if (rc) return rc;
-        kernel<<<grid, kThreads + 32, smem, static_cast<cudaStream_t>(stream)>>>(
-            static_cast<const TIn *>(input), codes, scales, static_cast<TOut *>(output), ta, ep);
-        rc = check_cuda(cudaGetLastError(), name);
-        return rc ? rc : ok();
-    }
+    const StreamMats mats = one_matrix(codes, scales, output, rows);
+    if (stream_plan(mats, n, tokens, ta, grid, smem))
+        return launch_stream<TIn, TOut>(input, mats, ta, grid, smem, ep, stream, name);
     const uint32_t ctas = (rows + kRowsPerCta - 1) / kRowsPerCta;
     nvfp4_matvec_kernel<TIn, TOut><<<ctas, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const TIn *>(input), codes, scales, static_cast<TOut *>(output), tokens, rows, n, ep);
@@ -556,4 +599,49 @@ extern "C" int apex_matmul_nvfp4_rms_norm(const void *input, int input_bf16, con
                                                             stream, name)
                       : launch_matvec<float, float>(input, codes, scales, output, hidden_dim, w_rows, tokens, ep,
                                                     stream, name);
+}
+
+extern "C" int apex_matmul_nvfp4_multi(const void *input, int input_bf16, uint32_t count,
+                                       const uint32_t *const *codes, const uint8_t *const *scales,
+                                       void *const *outputs, const uint32_t *w_rows, int output_bf16,
+                                       uint32_t hidden_dim, uint32_t tokens, void *stream) {
+    using namespace apex;
+    const char *name = "apex_matmul_nvfp4_multi";
+    if (count == 0) return ok();
+    if (count > static_cast<uint32_t>(kMaxMats))
+        return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": at most 4 matrices");
+    if (!codes || !scales || !outputs || !w_rows) return fail(APEX_ERR_INVALID_ARGUMENT, std::string(name) + ": null array");
+    StreamMats mats{};
+    mats.count = count;
+    for (uint32_t m = 0; m < count; ++m) {
+        const int rc = check_matvec(input, codes[m], scales[m], outputs[m], hidden_dim, w_rows[m], tokens,
+                                    input_bf16 != 0, name);
+        if (rc) return rc;
+        mats.codes[m] = codes[m];
+        mats.scales[m] = scales[m];
+        mats.out[m] = outputs[m];
+        mats.rows[m] = w_rows[m];
+        mats.tile0[m + 1] = mats.tile0[m] + (w_rows[m] + kTileRows - 1) / kTileRows;
+    }
+    if (tokens == 0 || mats.tile0[count] == 0) return ok();
+    TileArgs ta{};
+    uint32_t grid = 0;
+    size_t smem = 0;
+    bool empty_matrix = false;
+    for (uint32_t m = 0; m < count; ++m) empty_matrix = empty_matrix || w_rows[m] == 0;
+    if (!empty_matrix && stream_plan(mats, hidden_dim, tokens, ta, grid, smem)) {
+        const NormEpilogue none{};
+        if (input_bf16)
+            return output_bf16 ? launch_stream<__nv_bfloat16, __nv_bfloat16>(input, mats, ta, grid, smem, none, stream, name)
+                               : launch_stream<__nv_bfloat16, float>(input, mats, ta, grid, smem, none, stream, name);
+        return output_bf16 ? launch_stream<float, __nv_bfloat16>(input, mats, ta, grid, smem, none, stream, name)
+                           : launch_stream<float, float>(input, mats, ta, grid, smem, none, stream, name);
+    }
+    // shapes the streaming form does not take: one launch per matrix
+    for (uint32_t m = 0; m < count; ++m) {
+        const int rc = apex_matmul_nvfp4(input, input_bf16, codes[m], scales[m], outputs[m], output_bf16, hidden_dim,
+                                         w_rows[m], tokens, stream);
+        if (rc) return rc;
+    }
+    return ok();
 }

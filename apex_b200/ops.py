@@ -348,6 +348,35 @@ def matmul_nvfp4(input: torch.Tensor, W: Nvfp4Matrix, output: torch.Tensor, toke
     return output
 
 
+def matmul_nvfp4_multi(input: torch.Tensor, Ws, outputs, tokens: int):
+    """Up to four matmul_nvfp4 of the same input in one launch (q, k and v of a layer): outputs[m]
+    [tokens, Ws[m].w_rows] = Ws[m] . input[t], all outputs of one dtype (float32 or bfloat16)."""
+    Ws, outputs = list(Ws), list(outputs)
+    if not 1 <= len(Ws) <= 4 or len(outputs) != len(Ws):
+        raise ValueError("matmul_nvfp4_multi: one to four matrices, one output each")
+    if input.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("matmul_nvfp4_multi: input float32 or bfloat16")
+    out_dtype = outputs[0].dtype
+    if out_dtype not in (torch.float32, torch.bfloat16) or any(o.dtype != out_dtype for o in outputs):
+        raise TypeError("matmul_nvfp4_multi: outputs all float32 or all bfloat16")
+    n = Ws[0].hidden_dim
+    for W, o in zip(Ws, outputs):
+        _check_matrix(W)
+        if W.hidden_dim != n or o.numel() != tokens * W.w_rows:
+            raise ValueError("matmul_nvfp4_multi: same hidden_dim for every matrix, outputs [tokens, w_rows]")
+    if input.numel() != tokens * n:
+        raise ValueError("matmul_nvfp4_multi: input [tokens, hidden_dim]")
+    k = len(Ws)
+    codes = (ctypes.c_void_p * k)(*[W.codes.data_ptr() for W in Ws])
+    scales = (ctypes.c_void_p * k)(*[W.scales.data_ptr() for W in Ws])
+    outs = (ctypes.c_void_p * k)(*[ctypes_ptr(o) for o in outputs])
+    rows = (ctypes.c_uint32 * k)(*[W.w_rows for W in Ws])
+    check(_native.load().apex_matmul_nvfp4_multi(ctypes_ptr(input), int(input.dtype == torch.bfloat16), k, codes,
+                                                 scales, outs, rows, int(out_dtype == torch.bfloat16), n, tokens,
+                                                 _stream()))
+    return outputs
+
+
 def rms_norm(input: torch.Tensor, weights: torch.Tensor, result: torch.Tensor, rows: int, hidden_dim: int,
              eps: float) -> torch.Tensor:
     """apex::rmsNorm (src/ops.h:18-27): f32 rows [rows, hidden_dim], weights bf16 [hidden_dim]."""

@@ -500,8 +500,9 @@ class ProjWorkload:
     (docs/B6_3_attention.md:46-60): q (4096 x 2816), k and v (2048 x 2816) from the f32 normed
     hidden state to bf16 raw rows (what the fused decode takes), and o_proj (2816 x 4096) over the
     bf16 attention output with the post-attention RMSNorm fused in its epilogue.  NVFP4 weights
-    (E2M1 codes, E4M3 per-16 scales); one step = the four calls; algorithmic bytes = weight codes +
-    scales + activations.  N > 1: replicas."""
+    (E2M1 codes, E4M3 per-16 scales); one step = q, k and v in one launch (apex_matmul_nvfp4_multi:
+    they share the input) and the fused o_proj; algorithmic bytes = weight codes + scales +
+    activations.  N > 1: replicas."""
     kind = "proj"
     SHAPES = (("q", 4096, 2816), ("k", 2048, 2816), ("v", 2048, 2816), ("o", 2816, 4096))
 
@@ -531,14 +532,12 @@ class ProjWorkload:
         self.bytes = wbytes + 2816 * 4 + 4096 * 2 + (4096 + 2048 * 2) * 2 + 2816 * 4
         self.units = self.bytes
         self.tokens = 1
-        self.launches_per_step = 4
-        self.kernel_name = "nvfp4_stream_kernel (q, k, v, fused o_proj + rms_norm)"
+        self.launches_per_step = 2
+        self.kernel_name = "nvfp4_stream_kernel (q+k+v in one launch, fused o_proj + rms_norm)"
 
     def _run(self, W, x, att, q, k, v, o):
         ops = self.ops
-        ops.matmul_nvfp4(x, W["q"], q, 1)
-        ops.matmul_nvfp4(x, W["k"], k, 1)
-        ops.matmul_nvfp4(x, W["v"], v, 1)
+        ops.matmul_nvfp4_multi(x, [W["q"], W["k"], W["v"]], [q, k, v], 1)
         ops.matmul_nvfp4_rms_norm(att, W["o"], self.nw, o, 1, 1e-6, self.ws)
 
     def step(self, i):

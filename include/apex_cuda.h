@@ -303,6 +303,13 @@ APEX_API int apex_matmul_nvfp4_f32(const float *input, const uint32_t *codes, co
 APEX_API int apex_matmul_nvfp4(const void *input, int input_bf16, const uint32_t *codes, const uint8_t *scales,
                                void *output, int output_bf16, uint32_t hidden_dim, uint32_t w_rows, uint32_t tokens,
                                void *stream);
+/* Up to four projections of the same input in one launch (q, k and v of a layer: the reference's
+ * three matmulNvfp4 calls on one normed hidden state, src/ops.h:34-46): matrix m is codes[m] /
+ * scales[m] with w_rows[m] rows of hidden_dim, written to outputs[m] ([tokens][w_rows[m]]); every
+ * output is what apex_matmul_nvfp4 would write.  Arrays are host arrays of count entries. */
+APEX_API int apex_matmul_nvfp4_multi(const void *input, int input_bf16, uint32_t count, const uint32_t *const *codes,
+                                     const uint8_t *const *scales, void *const *outputs, const uint32_t *w_rows,
+                                     int output_bf16, uint32_t hidden_dim, uint32_t tokens, void *stream);
 /* rms_norm_f32 (shaders/norm.metal:36-81, apex::rmsNorm, src/ops.h:18-27): result[r] =
  * input[r] * rsqrt(mean(input[r]^2) + eps) * weight, rows of hidden_dim f32, weight bf16 bits. */
 APEX_API int apex_rms_norm_f32(const float *input, const uint16_t *weight, float *result, uint32_t rows,

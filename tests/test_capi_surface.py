@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared():
         assert name in syms, name
         assert getattr(lib, name) is not None
-    assert lib.apex_cuda_abi_version() == 102
+    assert lib.apex_cuda_abi_version() == 103
 
 
 def _params(**kw):

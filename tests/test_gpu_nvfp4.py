@@ -114,3 +114,32 @@ def test_oproj_post_norm_token_counts(tokens):
     ops.matmul_nvfp4_rms_norm(dev_bf16(xb).view(tokens, n), dev_matrix(codes, scales), dev_bf16(w), out, tokens, 1e-6, ws)
     ops.device_status()
     assert rel_l2(out.cpu().numpy(), ref) < REL_L2
+
+
+@pytest.mark.parametrize("shapes,n,tokens,bf16", [
+    (((4096, 1), (2048, 1), (2048, 1)), 2816, 1, True),     # q, k, v of a sliding layer (bf16 in and out)
+    (((64, 1), (48, 1), (37, 1)), 256, 1, False),           # ragged last tiles, one stage per matrix
+    (((100, 1), (64, 1)), 2816, 4, False),                  # several tokens
+    (((40, 1), (24, 1), (16, 1), (8, 1)), 96, 3, False),   # rows not filling tiles at n % 256 != 0: one launch each
+])
+def test_matmul_nvfp4_multi_equals_single_calls(shapes, n, tokens, bf16):
+    """One launch over several matrices of the same input writes what one apex_matmul_nvfp4 per
+    matrix writes (same per-row sums in the same order: bit-identical), and the f32 outputs meet the
+    oracle."""
+    mats = [oracle.nvfp4_matrix(r, n, 500 + i) for i, (r, _) in enumerate(shapes)]
+    x = np.random.default_rng(n + tokens).standard_normal((tokens, n)).astype(np.float32)
+    dt = torch.bfloat16 if bf16 else torch.float32
+    xd = torch.from_numpy(x).cuda().to(dt)
+    Ws = [dev_matrix(c, s) for c, s in mats]
+    multi = [torch.full((tokens, r), float("nan"), dtype=dt, device="cuda") for r, _ in shapes]
+    single = [torch.empty((tokens, r), dtype=dt, device="cuda") for r, _ in shapes]
+    ops.matmul_nvfp4_multi(xd, Ws, multi, tokens)
+    for W, o in zip(Ws, single):
+        ops.matmul_nvfp4(xd, W, o, tokens)
+    torch.cuda.synchronize()
+    ops.device_status()
+    for (r, _), (c, s), a, b in zip(shapes, mats, multi, single):
+        assert torch.equal(a.view(torch.int16) if bf16 else a, b.view(torch.int16) if bf16 else b)
+        if not bf16:
+            ref = oracle.matvec_nvfp4(c, s, x, tokens, r, n, ref=True)
+            assert rel_l2(a.cpu().numpy(), ref) < REL_L2
