@@ -76,6 +76,10 @@ CONFIGS = {
     "proj_decode": AttnConfig(
         "proj_decode", "proj", batch=1, seed=9, rope_theta=1e4,
         note="q/k/v and o_proj + post-attention norm of one decode token, sliding-layer shapes"),
+    # the same four projections over one 4096-token prefill chunk (the chunk of c4), bf16 activations
+    "proj_prefill": AttnConfig(
+        "proj_prefill", "proj", batch=1, seed=10, rope_theta=1e4, seq_len=4096, chunk=4096,
+        note="q/k/v and o_proj + post-attention norm of one 4096-token chunk, sliding-layer shapes"),
 }
 
 

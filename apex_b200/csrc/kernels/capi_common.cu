@@ -111,6 +111,24 @@ int make_tensor_map_bf16_3d(CUtensorMap *map, const void *base, uint64_t d0, uin
     return APEX_OK;
 }
 
+int make_tensor_map_u8_2d(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1, uint64_t stride1_bytes,
+                          uint32_t box0, uint32_t box1) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(APEX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {d0, d1};
+    const cuuint64_t strides[1] = {stride1_bytes};
+    const cuuint32_t box[2] = {box0, box1};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estride,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(APEX_ERR_INVALID_ARGUMENT,
+                    "cuTensorMapEncodeTiled rejected the tensor (error " + std::to_string((int)r) +
+                        "): base must be 16-byte aligned and strides multiples of 16 bytes");
+    return APEX_OK;
+}
+
 int make_tensor_map_bf16_3d_box(CUtensorMap *map, const void *base, const uint64_t (&dims)[3],
                                 const uint64_t (&strides_bytes)[2], const uint32_t (&box)[3]) {
     EncodeTiledFn fn = encode_fn();

@@ -206,6 +206,16 @@ __device__ __forceinline__ void tma_bulk_load(uint32_t dst, const void *src, uin
 }
 // 3-D tiled tensor load (no multicast).  c0 is the innermost coordinate in elements; it must
 // be a multiple of 16 bytes / element size.
+// 2-D tiled load global -> shared (this CTA), completing on `bar`; no multicast.  c0 * element size
+// must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t c0, int32_t c1,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+        : "memory");
+}
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int32_t c0,
                                             int32_t c1, int32_t c2, uint32_t bar) {
     asm volatile(

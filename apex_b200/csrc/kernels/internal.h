@@ -28,6 +28,11 @@ int make_tensor_map_bf16_3d(CUtensorMap *map, const void *base, uint64_t d0, uin
                             uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
                             uint32_t box0, uint32_t box1);
 
+// A 2-D byte tensor map, no swizzle: dims {d0 (innermost, bytes), d1}, byte stride of dim 1, box
+// {box0, box1} (box0 a multiple of 16 bytes).
+int make_tensor_map_u8_2d(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1, uint64_t stride1_bytes,
+                          uint32_t box0, uint32_t box1);
+
 // A 3-D bf16 tensor map with 128-byte swizzle and a full 3-D box: dims {d0 (innermost, elements),
 // d1, d2}, byte strides of dims 1 and 2 (any order), box {box0, box1, box2}.  Out-of-range elements read
 // as zero.

@@ -25,6 +25,7 @@
 
 #include <algorithm>
 #include <string>
+#include <type_traits>
 
 #include "common.cuh"
 #include "internal.h"
@@ -455,6 +456,230 @@ int check_matvec(const void *input, const uint32_t *codes, const uint8_t *scales
     return APEX_OK;
 }
 
+// ---------------------------------------------------------------- tensor-core form (prefill sizes)
+// For bf16 input and at least kTcMinTokens tokens the projection is a GEMM: D[r][t] = sum_k W[r][k]
+// x[t][k] with M = weight rows (128 per CTA), N = tokens (256 per CTA), K = hidden_dim (64 per
+// stage).  Weights stay NVFP4 in HBM; four warps dequantise each 128 x 64 tile exactly into bf16
+// (an E2M1 value times its E4M3 scale has at most 6 significant bits, so the bf16 product is exact)
+// and write it in the 128-byte-swizzled K-major layout a TMA copy would produce; x tiles come by
+// TMA.  One thread issues tcgen05.mma kind::f16 (f32 accumulate in TMEM, 256 columns); the same
+// four warps then read D back (TMEM lane = weight row, column = token) and store each token's 32
+// consecutive rows per instruction.  Sums are f32 over exact products (the order differs from the
+// per-group reference order by f32 rounding only).
+constexpr uint32_t kTcBM = 128, kTcBN = 256, kTcBK = 64, kTcStages = 4;
+constexpr uint32_t kTcMinTokens = 32;
+constexpr uint32_t kTcABytes = kTcBM * kTcBK * 2;            // 16 KB dequantised weights
+constexpr uint32_t kTcBBytes = kTcBN * kTcBK * 2;            // 32 KB activations
+constexpr uint32_t kTcRawBytes = kTcBM * (kTcBK / 2);        // 4 KB codes
+constexpr uint32_t kTcOffA = 0, kTcOffB = kTcStages * kTcABytes, kTcOffRaw = kTcOffB + kTcStages * kTcBBytes;
+constexpr uint32_t kTcOffBar = kTcOffRaw + kTcStages * kTcRawBytes;
+constexpr uint32_t kTcOffTmem = kTcOffBar + 8 * (3 * kTcStages + 1);
+constexpr uint32_t kTcSmem = kTcOffTmem + 16 + 1024;         // + alignment slack of the dynamic base
+constexpr int kTcThreads = 192;                              // warp 0 TMA, 1 MMA, 2-5 dequant + epilogue
+static_assert(kTcSmem <= 232448, "shared memory budget");
+
+struct TcArgs {
+    const uint8_t *scales;
+    void *out;
+    unsigned *status;
+    uint32_t rows, n, tokens;
+};
+
+template <typename TOut>
+__global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
+                                                                 const __grid_constant__ CUtensorMap tm_codes,
+                                                                 const TcArgs a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const uint32_t sb = smem_u32(base);
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t row0 = blockIdx.x * kTcBM, tok0 = blockIdx.y * kTcBN;
+    const uint32_t nk = a.n / kTcBK;
+    auto full_b = [&](uint32_t s) { return sb + kTcOffBar + 8 * s; };                   // x + codes landed
+    auto full_a = [&](uint32_t s) { return sb + kTcOffBar + 8 * (kTcStages + s); };     // A tile written
+    auto empty = [&](uint32_t s) { return sb + kTcOffBar + 8 * (2 * kTcStages + s); };  // MMA done with it
+    const uint32_t done = sb + kTcOffBar + 8 * (3 * kTcStages);
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(base + kTcOffTmem);
+    __shared__ int err;
+
+    if (tid == 0) {
+        prefetch_tensormap(&tm_x);
+        prefetch_tensormap(&tm_codes);
+        for (uint32_t s = 0; s < kTcStages; ++s) {
+            mbar_init(full_b(s), 1);
+            mbar_init(full_a(s), 4);
+            mbar_init(empty(s), 1);
+        }
+        mbar_init(done, 1);
+        err = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_holder), kTcBN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    bool alive = true;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            for (uint32_t kb = 0; kb < nk; ++kb) {
+                const uint32_t s = kb % kTcStages;
+                if (kb >= kTcStages && !mbar_wait(empty(s), ((kb / kTcStages) - 1) & 1, a.status)) {
+                    alive = false;
+                    break;
+                }
+                // full boxes (rows or tokens past the end read as zeros) complete the byte count
+                mbar_arrive_expect_tx(full_b(s), kTcBBytes + kTcRawBytes);
+                tma_load_3d(sb + kTcOffB + s * kTcBBytes, &tm_x, static_cast<int32_t>(kb * kTcBK),
+                            static_cast<int32_t>(tok0), 0, full_b(s));
+                tma_load_2d(sb + kTcOffRaw + s * kTcRawBytes, &tm_codes, static_cast<int32_t>(kb * (kTcBK / 2)),
+                            static_cast<int32_t>(row0), full_b(s));
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16_f32(kTcBM, kTcBN, 0, 0);
+            const uint64_t a_desc = smem_desc_sw128(sb + kTcOffA, 16, 1024);
+            const uint64_t b_desc = smem_desc_sw128(sb + kTcOffB, 16, 1024);
+            for (uint32_t kb = 0; kb < nk; ++kb) {
+                const uint32_t s = kb % kTcStages, ph = (kb / kTcStages) & 1;
+                if (!mbar_wait(full_b(s), ph, a.status) || !mbar_wait(full_a(s), ph, a.status)) {
+                    alive = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (uint32_t kk = 0; kk < kTcBK / 16; ++kk)  // K = 16 per MMA: +32 bytes inside the swizzle atom
+                    tc_mma_ss(tmem, a_desc + ((s * kTcABytes + kk * 32) >> 4), b_desc + ((s * kTcBBytes + kk * 32) >> 4),
+                              idesc, (kb | kk) ? 1u : 0u);
+                tc_commit(empty(s));
+            }
+            if (alive) tc_commit(done);
+        }
+    } else {
+        // ------------------------------------------------------------ dequantise, then epilogue
+        const uint32_t d = tid - 64;  // row of the tile this thread dequantises
+        const uint32_t grow = row0 + d;
+        const bool row_ok = grow < a.rows;
+        const uint8_t *srow = a.scales + static_cast<uint64_t>(row_ok ? grow : 0) * (a.n / 16);
+        // the 4 scales of a 64-wide step are one aligned 32-bit word; the next step's is loaded ahead
+        uint32_t sc_next = row_ok ? __ldg(reinterpret_cast<const uint32_t *>(srow)) : 0u;
+        for (uint32_t kb = 0; kb < nk; ++kb) {
+            const uint32_t s = kb % kTcStages;
+            const uint32_t sc = sc_next;
+            if (kb + 1 < nk) sc_next = row_ok ? __ldg(reinterpret_cast<const uint32_t *>(srow + 4 * (kb + 1))) : 0u;
+            if ((kb >= kTcStages && !mbar_wait(empty(s), ((kb / kTcStages) - 1) & 1, a.status)) ||
+                !mbar_wait(full_b(s), (kb / kTcStages) & 1, a.status)) {
+                alive = false;
+                break;
+            }
+            const uint4 *raw = reinterpret_cast<const uint4 *>(base + kTcOffRaw + s * kTcRawBytes + d * (kTcBK / 2));
+            const uint4 c0 = raw[0], c1 = raw[1];
+            const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            const uint32_t arow = sb + kTcOffA + s * kTcABytes + d * 128;  // 1024-aligned tile: row d's 128 B
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {  // 16 weights per group, its E4M3 scale
+                float w[16];
+                decode_group(make_uint2(words[2 * g], words[2 * g + 1]), w);
+                const float scale = e4m3_to_f32(static_cast<uint8_t>((sc >> (8 * g)) & 0xFFu));
+                uint32_t pk[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) pk[i] = pack_bf16(w[2 * i] * scale, w[2 * i + 1] * scale);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)  // 16-byte chunk c of the row at (c ^ (row & 7)) * 16
+                    st_shared_v4(arow + (((2 * g + h) ^ (d & 7)) << 4),
+                                 make_uint4(pk[4 * h], pk[4 * h + 1], pk[4 * h + 2], pk[4 * h + 3]));
+            }
+            fence_proxy_async_smem();  // the tensor cores read the tile through the async proxy
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full_a(s));
+        }
+        if (alive && !mbar_wait(done, 0, a.status)) alive = false;
+        if (alive) {
+            tc_fence_after();
+            const uint32_t q = warp & 3;  // TMEM lanes 32q.. (weight rows 32q.. of the tile)
+            const uint32_t row = row0 + 32 * q + lane;
+            const uint32_t taddr = tmem + ((32u * q) << 16);
+            TOut *out = static_cast<TOut *>(a.out);
+#pragma unroll 1
+            for (uint32_t j = 0; j < kTcBN / 32; ++j) {
+                if (tok0 + 32 * j >= a.tokens) break;  // warp-uniform
+                uint32_t v[32];
+                tmem_ld32(taddr + 32 * j, v);
+                tc_wait_ld(v);
+                if (row < a.rows) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const uint32_t t = tok0 + 32 * j + i;
+                        if (t < a.tokens) store(out + static_cast<uint64_t>(t) * a.rows + row, __uint_as_float(v[i]));
+                    }
+                }
+            }
+        }
+    }
+    if (!alive) err = 1;
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && err) {  // copies or MMAs may still be in flight after a failed wait
+        const long long start = clock64();
+        while (clock64() - start < 400000ll) __nanosleep(1000);
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTcBN);
+    }
+}
+
+template <typename TOut>
+int launch_tc(const void *input, const uint32_t *codes, const uint8_t *scales, void *output, uint32_t n, uint32_t rows,
+              uint32_t tokens, void *stream, const char *name) {
+    CUtensorMap tx, tcodes;
+    // x [tokens][n] bf16: one box = 256 tokens x 64 elements (128-byte swizzle, K-major)
+    int rc = make_tensor_map_bf16_3d(&tx, input, n, tokens, 1, n * 2ull, n * 2ull * tokens, kTcBK, kTcBN);
+    if (rc) return rc;
+    // codes [rows][n/2] bytes: one box = 128 rows x 32 bytes (64 weights)
+    rc = make_tensor_map_u8_2d(&tcodes, codes, n / 2, rows, n / 2, kTcBK / 2, kTcBM);
+    if (rc) return rc;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        rc = check_cuda(cudaFuncSetAttribute(nvfp4_tc_kernel<TOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kTcSmem)),
+                        name);
+        if (rc) return rc;
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    TcArgs ta{};
+    ta.scales = scales;
+    ta.out = output;
+    ta.status = device_status_ptr();
+    if (!ta.status) return fail(APEX_ERR_CUDA, std::string(name) + ": device status word unavailable");
+    ta.rows = rows;
+    ta.n = n;
+    ta.tokens = tokens;
+    const dim3 grid((rows + kTcBM - 1) / kTcBM, (tokens + kTcBN - 1) / kTcBN);
+    nvfp4_tc_kernel<TOut><<<grid, kTcThreads, kTcSmem, static_cast<cudaStream_t>(stream)>>>(tx, tcodes, ta);
+    rc = check_cuda(cudaGetLastError(), name);
+    return rc ? rc : ok();
+}
+
+// The tensor-core form applies to bf16 input from kTcMinTokens tokens, hidden_dim a multiple of 64,
+// 16-byte aligned input and codes and 4-byte aligned scales.
+bool tc_applies(bool in_bf16, const void *input, const uint32_t *codes, const uint8_t *scales, uint32_t n,
+                uint32_t tokens, uint32_t rows) {
+    return in_bf16 && tokens >= kTcMinTokens && n % kTcBK == 0 && rows > 0 && tokens <= 65535u * kTcBN &&
+           !(reinterpret_cast<uintptr_t>(input) & 15) && !(reinterpret_cast<uintptr_t>(codes) & 15) &&
+           !(reinterpret_cast<uintptr_t>(scales) & 3);
+}
+
 // The streaming form applies when every tile's codes and scales are whole 16-byte runs at 16-byte
 // offsets (n a multiple of 32, and of 256 unless the rows fill whole tiles) and two stages fit.
 bool stream_plan(const StreamMats &mats, uint32_t n, uint32_t tokens, TileArgs &ta, uint32_t &grid, size_t &smem) {
@@ -510,6 +735,8 @@ int launch_matvec(const void *input, const uint32_t *codes, const uint8_t *scale
     TileArgs ta{};
     uint32_t grid = 0;
     size_t smem = 0;
+    if (!ep.weight && tc_applies(std::is_same<TIn, __nv_bfloat16>::value, input, codes, scales, n, tokens, rows))
+        return launch_tc<TOut>(input, codes, scales, output, n, rows, tokens, stream, name);
     const StreamMats mats = one_matrix(codes, scales, output, rows);
     if (stream_plan(mats, n, tokens, ta, grid, smem))
         return launch_stream<TIn, TOut>(input, mats, ta, grid, smem, ep, stream, name);
@@ -627,9 +854,13 @@ extern "C" int apex_matmul_nvfp4_multi(const void *input, int input_bf16, uint32
     TileArgs ta{};
     uint32_t grid = 0;
     size_t smem = 0;
-    bool empty_matrix = false;
-    for (uint32_t m = 0; m < count; ++m) empty_matrix = empty_matrix || w_rows[m] == 0;
-    if (!empty_matrix && stream_plan(mats, hidden_dim, tokens, ta, grid, smem)) {
+    bool empty_matrix = false, tensor_core = true;
+    for (uint32_t m = 0; m < count; ++m) {
+        empty_matrix = empty_matrix || w_rows[m] == 0;
+        tensor_core = tensor_core && tc_applies(input_bf16 != 0, input, codes[m], scales[m], hidden_dim, tokens, w_rows[m]);
+    }
+    // prefill sizes: one tensor-core GEMM per matrix (below) instead of the streaming walk
+    if (!empty_matrix && !tensor_core && stream_plan(mats, hidden_dim, tokens, ta, grid, smem)) {
         const NormEpilogue none{};
         if (input_bf16)
             return output_bf16 ? launch_stream<__nv_bfloat16, __nv_bfloat16>(input, mats, ta, grid, smem, none, stream, name)
@@ -637,7 +868,7 @@ extern "C" int apex_matmul_nvfp4_multi(const void *input, int input_bf16, uint32
         return output_bf16 ? launch_stream<float, __nv_bfloat16>(input, mats, ta, grid, smem, none, stream, name)
                            : launch_stream<float, float>(input, mats, ta, grid, smem, none, stream, name);
     }
-    // shapes the streaming form does not take: one launch per matrix
+    // prefill sizes, or shapes the streaming form does not take: one launch per matrix
     for (uint32_t m = 0; m < count; ++m) {
         const int rc = apex_matmul_nvfp4(input, input_bf16, codes[m], scales[m], outputs[m], output_bf16, hidden_dim,
                                          w_rows[m], tokens, stream);

@@ -57,7 +57,7 @@ from apex_b200.configs import CONFIGS, decode_bytes, prefill_flops, visible_pair
 
 PRIMARY = "c5_long_decode_b8"
 ALSO = ("c1_decode", "c2_prefill_window", "c3_ragged_decode", "c4_chunked_prefill", "c5_long_decode_b1",
-        "global_decode", "proj_decode")
+        "global_decode", "proj_decode", "proj_prefill")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_BYTES = 126 * 1024 * 1024
 TOL_MAX, TOL_MEAN = 2e-2, 2e-3          # against an fp32 reference
@@ -496,13 +496,16 @@ class DecodeWorkload:
 
 
 class ProjWorkload:
-    """The projections either side of one decode step of a sliding layer of the reference model
-    (docs/B6_3_attention.md:46-60): q (4096 x 2816), k and v (2048 x 2816) from the f32 normed
-    hidden state to bf16 raw rows (what the fused decode takes), and o_proj (2816 x 4096) over the
-    bf16 attention output with the post-attention RMSNorm fused in its epilogue.  NVFP4 weights
-    (E2M1 codes, E4M3 per-16 scales); one step = q, k and v in one launch (apex_matmul_nvfp4_multi:
-    they share the input) and the fused o_proj; algorithmic bytes = weight codes + scales +
-    activations.  N > 1: replicas."""
+    """The projections either side of one attention step of a sliding layer of the reference model
+    (docs/B6_3_attention.md:46-60): q (4096 x 2816), k and v (2048 x 2816) from the normed hidden
+    state to bf16 raw rows (what the fused attention takes), and o_proj (2816 x 4096) over the bf16
+    attention output with the post-attention RMSNorm.  NVFP4 weights (E2M1 codes, E4M3 per-16
+    scales).  proj_decode: one token, f32 hidden state (the reference's), q, k and v in one launch
+    (apex_matmul_nvfp4_multi: they share the input) and o_proj with the norm fused into its epilogue;
+    algorithmic bytes = weight codes + scales + activations.  proj_prefill: one 4096-token chunk of
+    bf16 activations on the tensor-core form (each projection one tcgen05 GEMM over exactly
+    dequantised weights), the norm a second launch; algorithmic work = 2 x tokens x weights FLOPs.
+    N > 1: replicas."""
     kind = "proj"
     SHAPES = (("q", 4096, 2816), ("k", 2048, 2816), ("v", 2048, 2816), ("o", 2816, 4096))
 
@@ -511,6 +514,8 @@ class ProjWorkload:
         from apex_b200 import ops
         self.ops, self.torch, self.cfg = ops, torch, cfg
         self.sharding = "replica"
+        T = self.T = cfg.chunk or 1
+        self.prefill = T > 1
         g = torch.Generator(device=device).manual_seed(900 + rank)
         wbytes = sum(r * n // 2 + r * n // 16 for _, r, n in self.SHAPES)
         self.R = max(2, math.ceil(2 * L2_BYTES / wbytes) + 1)
@@ -521,34 +526,41 @@ class ProjWorkload:
             return ops.Nvfp4Matrix(codes, scales)
 
         self.sets = [{k: matrix(r, n) for k, r, n in self.SHAPES} for _ in range(self.R)]
-        self.x = torch.randn(1, 2816, generator=g, device=device)
-        self.att = torch.randn(1, 4096, generator=g, device=device).to(torch.bfloat16)
+        x_dtype = torch.bfloat16 if self.prefill else torch.float32
+        self.x = torch.randn(T, 2816, generator=g, device=device).to(x_dtype)
+        self.att = torch.randn(T, 4096, generator=g, device=device).to(torch.bfloat16)
         self.nw = (torch.randn(2816, generator=g, device=device) * 0.1 + 1.0).to(torch.bfloat16)
-        self.q = torch.empty(1, 4096, dtype=torch.bfloat16, device=device)
-        self.k = torch.empty(1, 2048, dtype=torch.bfloat16, device=device)
-        self.v = torch.empty(1, 2048, dtype=torch.bfloat16, device=device)
-        self.o = torch.empty(1, 2816, device=device)
-        self.ws = ops.ProjNormWorkspace(2816, 1, device=device)
-        self.bytes = wbytes + 2816 * 4 + 4096 * 2 + (4096 + 2048 * 2) * 2 + 2816 * 4
-        self.units = self.bytes
-        self.tokens = 1
-        self.launches_per_step = 2
-        self.kernel_name = "nvfp4_stream_kernel (q+k+v in one launch, fused o_proj + rms_norm)"
+        self.q = torch.empty(T, 4096, dtype=torch.bfloat16, device=device)
+        self.k = torch.empty(T, 2048, dtype=torch.bfloat16, device=device)
+        self.v = torch.empty(T, 2048, dtype=torch.bfloat16, device=device)
+        self.o = torch.empty(T, 2816, device=device)
+        self.ws = ops.ProjNormWorkspace(2816, min(T, 16), device=device)
+        xb = self.x.element_size()
+        self.bytes = wbytes + T * (2816 * xb + 4096 * 2 + (4096 + 2048 * 2) * 2 + 2816 * 4)
+        self.flops = 2 * T * sum(r * n for _, r, n in self.SHAPES)
+        self.units = self.flops if self.prefill else self.bytes
+        self.tokens = T
+        if self.prefill:
+            self.launches_per_step = 5
+            self.kernel_name = "nvfp4_tc_kernel (q, k, v, o_proj: tcgen05 GEMMs) + rms_norm"
+        else:
+            self.launches_per_step = 2
+            self.kernel_name = "nvfp4_stream_kernel (q+k+v in one launch, fused o_proj + rms_norm)"
 
     def _run(self, W, x, att, q, k, v, o):
         ops = self.ops
-        ops.matmul_nvfp4_multi(x, [W["q"], W["k"], W["v"]], [q, k, v], 1)
-        ops.matmul_nvfp4_rms_norm(att, W["o"], self.nw, o, 1, 1e-6, self.ws)
+        ops.matmul_nvfp4_multi(x, [W["q"], W["k"], W["v"]], [q, k, v], self.T)
+        ops.matmul_nvfp4_rms_norm(att, W["o"], self.nw, o, self.T, 1e-6, self.ws)
 
     def step(self, i):
         self._run(self.sets[i % self.R], self.x, self.att, self.q, self.k, self.v, self.o)
 
     def dominant_launches(self, i, record):
         record(lambda: self.step(i))
-        return self.bytes
+        return self.units
 
     def roofline_work(self):
-        return self.bytes, "hbm"
+        return (self.flops, "tensor") if self.prefill else (self.bytes, "hbm")
 
     def e2e_inputs(self):
         return [self.x, self.att], self.o
@@ -579,12 +591,16 @@ class ProjWorkload:
         worst, rel = 0.0, 0.0
         for name, out in (("q", self.q), ("k", self.k), ("v", self.v)):
             ref = (dense(W[name]) @ self.x.double().T).T
-            err = ((out.double() - ref).abs() / ref.abs().clamp_min(1e-3)).max().item()
+            if self.prefill:  # millions of outputs, some near zero: the bf16 rounding as a relative L2
+                err = ((out.double() - ref).norm() / ref.norm()).item()
+            else:
+                err = ((out.double() - ref).abs() / ref.abs().clamp_min(1e-3)).max().item()
             worst = max(worst, err)
         ro = (dense(W["o"]) @ self.att.double().T).T
         ro = ro * torch.rsqrt((ro ** 2).mean(-1, keepdim=True) + 1e-6) * self.nw.double()
         rel = ((self.o.double() - ro).norm() / ro.norm()).item()
-        return {"max_abs": worst, "mean_abs": rel, "o_proj_norm_rel_l2": rel, "qkv_bf16_max_rel": worst,
+        key = "qkv_bf16_rel_l2" if self.prefill else "qkv_bf16_max_rel"
+        return {"max_abs": worst, "mean_abs": rel, "o_proj_norm_rel_l2": rel, key: worst,
                 "ref": "torch fp64: weights decoded from the E2M1 / E4M3 bits", "ok": rel < 1e-5 and worst <= 2 ** -8}
 
     def close(self):
@@ -629,19 +645,27 @@ def cpu_reference_step(cfg, threads):
     oracle.set_threads(threads)
     ref = oracle.ref_lib() is not None
     kind = "reference" if ref else "port"
-    if cfg.kind == "proj":  # matvecNvfp4Cpu on the four projections of one decode token, then rmsNormCpu
+    if cfg.kind == "proj":  # matvecNvfp4Cpu on the four projections, then rmsNormCpu
         key = ("proj",)
         if key not in _REF_CACHE:
             _REF_CACHE[key] = [oracle.nvfp4_matrix(r, n, 900 + i) + (r, n)
                                for i, (_, r, n) in enumerate(ProjWorkload.SHAPES)]
         mats = _REF_CACHE[key]
         nw = oracle.normal_bf16(2816, 900, 4, 0, 1.0, 0.1)
-        xs = {n: np.random.default_rng(n).standard_normal((1, n)).astype(np.float32) for _, _, n in ProjWorkload.SHAPES}
+        # prefill: a sample of 4 tokens of the chunk (bf16-valued activations), value = their FLOPs / time
+        T = 4 if cfg.chunk else 1
+        xs = {n: np.random.default_rng(n).standard_normal((T, n)).astype(np.float32) for _, _, n in ProjWorkload.SHAPES}
+        if cfg.chunk:
+            xs = {n: oracle.bf16_to_f32(oracle.f32_to_bf16(x.ravel())).reshape(T, n) for n, x in xs.items()}
         t0 = time.perf_counter()
         for codes, scales, r, n in mats:
-            y = oracle.matvec_nvfp4(codes, scales, xs[n], 1, r, n, ref=ref)
-        oracle.rms_norm_rows(y, nw, 1, 2816, 1e-6, ref=ref)
+            y = oracle.matvec_nvfp4(codes, scales, xs[n], T, r, n, ref=ref)
+        oracle.rms_norm_rows(y, nw, T, 2816, 1e-6, ref=ref)
         dt = time.perf_counter() - t0
+        if cfg.chunk:
+            flops = 2 * T * sum(r * n for _, r, n in ProjWorkload.SHAPES)
+            return dt, flops, (f"the four projections of {T} of the chunk's {cfg.chunk} tokens (matvecNvfp4Cpu) + "
+                               "rmsNormCpu; value = their FLOPs / time"), kind
         nbytes = sum(r * n // 2 + r * n // 16 for _, r, n in ProjWorkload.SHAPES)
         return dt, nbytes, "the four projections of one decode token (matvecNvfp4Cpu) + rmsNormCpu; value = weight bytes / time", kind
     Hq, Hkv, D = cfg.q_heads, cfg.kv_heads, cfg.head_dim
@@ -721,6 +745,8 @@ def metric_of(cfg):
     if cfg.kind == "prefill":
         return "prefill attn TFLOP/s", "TFLOP/s", 1e12
     if cfg.kind == "proj":
+        if cfg.chunk:
+            return "prefill projections TFLOP/s", "TFLOP/s", 1e12
         return "decode projections GB/s", "GB/s", 1e9
     return "decode attn KV GB/s", "GB/s", 1e9
 
@@ -734,8 +760,9 @@ def cpu_baseline(cfg, threads):
 
 def config_of(cfg):
     if cfg.kind == "proj":
-        return {"workload": cfg.name, "tokens": 1, "matrices": {k: [r, n] for k, r, n in ProjWorkload.SHAPES},
-                "weights": "NVFP4 (E2M1 codes, E4M3 per-16 scales)", "fused": "o_proj + post-attention rms_norm"}
+        return {"workload": cfg.name, "tokens": cfg.chunk or 1, "matrices": {k: [r, n] for k, r, n in ProjWorkload.SHAPES},
+                "weights": "NVFP4 (E2M1 codes, E4M3 per-16 scales)", "activations": "bf16" if cfg.chunk else "f32",
+                "fused": "o_proj + post-attention rms_norm"}
     c = {"workload": cfg.name, "batch": cfg.batch, "q_heads": cfg.q_heads, "kv_heads": cfg.kv_heads,
          "head_dim": cfg.head_dim, "window": cfg.window, "rope_theta": cfg.rope_theta,
          "qk_norm": cfg.qk_norm, "scale": "1/sqrt(head_dim)"}

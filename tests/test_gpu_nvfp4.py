@@ -143,3 +143,26 @@ def test_matmul_nvfp4_multi_equals_single_calls(shapes, n, tokens, bf16):
         if not bf16:
             ref = oracle.matvec_nvfp4(c, s, x, tokens, r, n, ref=True)
             assert rel_l2(a.cpu().numpy(), ref) < REL_L2
+
+
+@pytest.mark.parametrize("rows,n,tokens", [(128, 256, 32), (200, 2816, 100), (1024, 4096, 256), (512, 2816, 300),
+                                           (64, 512, 513)])
+def test_matmul_nvfp4_tensor_core_form_vs_oracle(rows, n, tokens):
+    """bf16 input from 32 tokens runs on tcgen05 (weights dequantised exactly to bf16 in shared memory,
+    f32 accumulation in TMEM): the reference's gate against the oracle on the same bf16 values, for
+    full and ragged row / token tiles, f32 and bf16 output."""
+    codes, scales = oracle.nvfp4_matrix(rows, n, 700 + rows)
+    xb = oracle.normal_bf16(tokens * n, 700 + tokens, 1)
+    x = oracle.bf16_to_f32(xb).reshape(tokens, n)
+    ref = oracle.matvec_nvfp4(codes, scales, x, tokens, rows, n, ref=True)
+    W = dev_matrix(codes, scales)
+    xd = dev_bf16(xb).view(tokens, n)
+    out32 = torch.full((tokens, rows), float("nan"), device="cuda")
+    ops.matmul_nvfp4(xd, W, out32, tokens)
+    torch.cuda.synchronize()
+    ops.device_status()
+    assert rel_l2(out32.cpu().numpy(), ref) < REL_L2
+    out16 = torch.empty(tokens, rows, dtype=torch.bfloat16, device="cuda")
+    ops.matmul_nvfp4(xd, W, out16, tokens)
+    # one bf16 rounding of each output; the absolute term covers f32 sums that cancel to near zero
+    np.testing.assert_allclose(out16.float().cpu().numpy(), ref, rtol=2 ** -8, atol=4e-6 * np.abs(ref).max())
