@@ -458,155 +458,250 @@ int check_matvec(const void *input, const uint32_t *codes, const uint8_t *scales
 
 // ---------------------------------------------------------------- tensor-core form (prefill sizes)
 // For bf16 input and at least kTcMinTokens tokens the projection is a GEMM: D[r][t] = sum_k W[r][k]
-// x[t][k] with M = weight rows (128 per CTA), N = tokens (256 per CTA), K = hidden_dim (64 per
-// stage).  Weights stay NVFP4 in HBM; four warps dequantise each 128 x 64 tile exactly into bf16
-// (an E2M1 value times its E4M3 scale has at most 6 significant bits, so the bf16 product is exact)
-// and write it in the 128-byte-swizzled K-major layout a TMA copy would produce; x tiles come by
-// TMA.  One thread issues tcgen05.mma kind::f16 (f32 accumulate in TMEM, 256 columns); the same
-// four warps then read D back (TMEM lane = weight row, column = token) and store each token's 32
-// consecutive rows per instruction.  Sums are f32 over exact products (the order differs from the
-// per-group reference order by f32 rounding only).
-constexpr uint32_t kTcBM = 128, kTcBN = 256, kTcBK = 64, kTcStages = 4;
+// x[t][k], M = weight rows, N = tokens, K = hidden_dim, run on CTA pairs (tcgen05.mma.cta_group::2,
+// M = 256: each CTA dequantises its own 128 weight rows).  A tile is 256 rows x 512 tokens: every
+// dequantised 64-wide K step of the weights feeds two N = 256 MMAs (the weights' dequantisation, not
+// the tensor cores, is the scarcer resource), and each CTA loads 256 of the 512 tokens (128 of each
+// MMA), so an SM streams 32 KB of activations and 4 KB of codes per K step.  Weights stay NVFP4 in
+// HBM; eight warps per CTA dequantise each 128 x 64 tile exactly into bf16 (an E2M1 value times its
+// E4M3 scale has at most 6 significant bits, so the bf16 product is exact) and write it in the
+// 128-byte-swizzled K-major layout a TMA copy would produce; x tiles and the codes come by TMA.
+// CTA 0's MMA warp issues tcgen05.mma kind::f16 (f32 accumulate in TMEM, all 512 columns); four
+// epilogue warps per CTA read each tile back (TMEM lane = weight row, column c = token tok0 + c;
+// each store writes 32 consecutive rows of one token).  The grid is persistent (pairs take tiles
+// round-robin, weight-row major so concurrent pairs share weight rows in L2).  Sums are f32 over
+// exact products (the order differs from the per-group reference order by f32 rounding only).
+// No TMA multicast.
+// Three rings per CTA: x halves (B, freed by the MMAs), dequantised weights (A, written by the
+// dequantising warps, freed by the MMAs) and raw codes (freed by the dequantising warps as soon as
+// they have read them, so the codes run far ahead of the MMAs and a dequantisation never waits for a
+// load issued after the MMA that freed its A slot).  The dequantising warps hand each A tile to CTA
+// 0's barrier after an async-proxy fence with a CTA-scope arrival (a cluster-scope release per warp
+// and step halved the kernel's rate).
+constexpr uint32_t kTcBM = 128, kTcBN = 512, kTcBK = 64;  // BM per CTA, BN per pair (two N = 256 MMAs)
+constexpr uint32_t kTcSB = 3, kTcSA = 4, kTcSR = 8;       // ring depths: x, A, codes
 constexpr uint32_t kTcMinTokens = 32;
 constexpr uint32_t kTcABytes = kTcBM * kTcBK * 2;            // 16 KB dequantised weights
-constexpr uint32_t kTcBBytes = kTcBN * kTcBK * 2;            // 32 KB activations
+constexpr uint32_t kTcBBytes = (kTcBN / 2) * kTcBK * 2;      // 32 KB: this CTA's half of the x tile
+constexpr uint32_t kTcBHalf = kTcBBytes / 2;                 // its 128 tokens of one N = 256 MMA
 constexpr uint32_t kTcRawBytes = kTcBM * (kTcBK / 2);        // 4 KB codes
-constexpr uint32_t kTcOffA = 0, kTcOffB = kTcStages * kTcABytes, kTcOffRaw = kTcOffB + kTcStages * kTcBBytes;
-constexpr uint32_t kTcOffBar = kTcOffRaw + kTcStages * kTcRawBytes;
-constexpr uint32_t kTcOffTmem = kTcOffBar + 8 * (3 * kTcStages + 1);
+constexpr uint32_t kTcOffA = 0, kTcOffB = kTcSA * kTcABytes, kTcOffRaw = kTcOffB + kTcSB * kTcBBytes;
+constexpr uint32_t kTcOffBar = kTcOffRaw + kTcSR * kTcRawBytes;
+constexpr uint32_t kTcNumBars = 2 * (kTcSB + kTcSA + kTcSR) + 2;
+constexpr uint32_t kTcOffTmem = kTcOffBar + 8 * kTcNumBars;
 constexpr uint32_t kTcSmem = kTcOffTmem + 16 + 1024;         // + alignment slack of the dynamic base
-constexpr int kTcThreads = 192;                              // warp 0 TMA, 1 MMA, 2-5 dequant + epilogue
+// warp 0 x loads, 1 MMA, 2-9 dequantise (two threads per row), 10-13 epilogue, 14 code loads
+constexpr int kTcThreads = 480;
+constexpr uint32_t kTcDqWarps = 8, kTcEpiWarps = 4, kTcCodeWarp = 14;
 static_assert(kTcSmem <= 232448, "shared memory budget");
 
 struct TcArgs {
     const uint8_t *scales;
     void *out;
     unsigned *status;
-    uint32_t rows, n, tokens;
+    uint32_t rows, n, tokens, tiles_n, tiles;
 };
 
 template <typename TOut>
-__global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
-                                                                 const __grid_constant__ CUtensorMap tm_codes,
-                                                                 const TcArgs a) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
+    nvfp4_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_codes,
+                    const TcArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     const uint32_t sb = smem_u32(base);
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t row0 = blockIdx.x * kTcBM, tok0 = blockIdx.y * kTcBN;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
     const uint32_t nk = a.n / kTcBK;
-    auto full_b = [&](uint32_t s) { return sb + kTcOffBar + 8 * s; };                   // x + codes landed
-    auto full_a = [&](uint32_t s) { return sb + kTcOffBar + 8 * (kTcStages + s); };     // A tile written
-    auto empty = [&](uint32_t s) { return sb + kTcOffBar + 8 * (2 * kTcStages + s); };  // MMA done with it
-    const uint32_t done = sb + kTcOffBar + 8 * (3 * kTcStages);
+    // CTA 0's b_full, a_full and acc_empty count the pair; the others are each CTA's own
+    auto bar_at = [&](uint32_t i) { return sb + kTcOffBar + 8 * i; };
+    auto b_full = [&](uint32_t s) { return bar_at(s); };                                   // x halves landed
+    auto b_empty = [&](uint32_t s) { return bar_at(kTcSB + s); };                          // MMAs done with them
+    auto a_full = [&](uint32_t s) { return bar_at(2 * kTcSB + s); };                       // A tiles written
+    auto a_empty = [&](uint32_t s) { return bar_at(2 * kTcSB + kTcSA + s); };              // MMAs done with it
+    auto raw_full = [&](uint32_t s) { return bar_at(2 * (kTcSB + kTcSA) + s); };           // codes landed
+    auto raw_empty = [&](uint32_t s) { return bar_at(2 * (kTcSB + kTcSA) + kTcSR + s); };  // codes read
+    const uint32_t acc_full = bar_at(2 * (kTcSB + kTcSA + kTcSR));
+    const uint32_t acc_empty = bar_at(2 * (kTcSB + kTcSA + kTcSR) + 1);
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(base + kTcOffTmem);
     __shared__ int err;
 
     if (tid == 0) {
         prefetch_tensormap(&tm_x);
         prefetch_tensormap(&tm_codes);
-        for (uint32_t s = 0; s < kTcStages; ++s) {
-            mbar_init(full_b(s), 1);
-            mbar_init(full_a(s), 4);
-            mbar_init(empty(s), 1);
+        for (uint32_t s = 0; s < kTcSB; ++s) {
+            mbar_init(b_full(s), 1);
+            mbar_init(b_empty(s), 1);
         }
-        mbar_init(done, 1);
+        for (uint32_t s = 0; s < kTcSA; ++s) {
+            mbar_init(a_full(s), 2 * kTcDqWarps);
+            mbar_init(a_empty(s), 1);
+        }
+        for (uint32_t s = 0; s < kTcSR; ++s) {
+            mbar_init(raw_full(s), 1);
+            mbar_init(raw_empty(s), kTcDqWarps);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 2 * kTcEpiWarps);
         err = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_holder), kTcBN);
-        tmem_relinquish();
+        tmem_alloc_pair(smem_u32(tmem_holder), kTcBN);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
     bool alive = true;
-
+    // the pair's tiles: pair, + pairs, ...; tile t = (256 weight rows t / tiles_n, 256 tokens t % tiles_n)
+    const uint32_t pair = blockIdx.x / 2, pairs = gridDim.x / 2;
+    auto tile_row0 = [&](uint32_t t) { return (t / a.tiles_n) * (2 * kTcBM) + rank * kTcBM; };  // this CTA's rows
+    auto tile_tok0 = [&](uint32_t t) { return (t % a.tiles_n) * kTcBN; };
     if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer
+        // ------------------------------------------------------------ x loads (each CTA its half)
         if (lane == 0) {
-            for (uint32_t kb = 0; kb < nk; ++kb) {
-                const uint32_t s = kb % kTcStages;
-                if (kb >= kTcStages && !mbar_wait(empty(s), ((kb / kTcStages) - 1) & 1, a.status)) {
-                    alive = false;
-                    break;
+            uint32_t g = 0;  // step counter over all tiles
+            const uint32_t bf0 = mapa(b_full(0), 0);
+            for (uint32_t t = pair; t < a.tiles && alive; t += pairs) {
+                // this CTA's 128 tokens of each N = 256 half: tok0 + 128 rank and tok0 + 256 + 128 rank
+                const int32_t x0 = static_cast<int32_t>(tile_tok0(t) + rank * 128);
+                for (uint32_t kb = 0; kb < nk; ++kb, ++g) {
+                    const uint32_t s = g % kTcSB;
+                    if (g >= kTcSB && !mbar_wait(b_empty(s), ((g / kTcSB) - 1) & 1, a.status)) {
+                        alive = false;
+                        break;
+                    }
+                    // both CTAs' halves complete on CTA 0's barrier (full boxes: tokens past the end
+                    // read as zeros)
+                    if (leader) mbar_arrive_expect_tx(b_full(s), 2 * kTcBBytes);
+                    for (uint32_t h = 0; h < 2; ++h)
+                        tma_load_3d_pair(sb + kTcOffB + s * kTcBBytes + h * kTcBHalf, &tm_x, static_cast<int32_t>(kb * kTcBK),
+                                         x0 + static_cast<int32_t>(256 * h), 0, bf0 + 8 * s);
                 }
-                // full boxes (rows or tokens past the end read as zeros) complete the byte count
-                mbar_arrive_expect_tx(full_b(s), kTcBBytes + kTcRawBytes);
-                tma_load_3d(sb + kTcOffB + s * kTcBBytes, &tm_x, static_cast<int32_t>(kb * kTcBK),
-                            static_cast<int32_t>(tok0), 0, full_b(s));
-                tma_load_2d(sb + kTcOffRaw + s * kTcRawBytes, &tm_codes, static_cast<int32_t>(kb * (kTcBK / 2)),
-                            static_cast<int32_t>(row0), full_b(s));
+            }
+        }
+    } else if (warp == kTcCodeWarp) {
+        // ------------------------------------------------------------ code loads (each CTA its rows)
+        if (lane == 0) {
+            uint32_t g = 0;
+            for (uint32_t t = pair; t < a.tiles && alive; t += pairs) {
+                const int32_t r0 = static_cast<int32_t>(tile_row0(t));
+                for (uint32_t kb = 0; kb < nk; ++kb, ++g) {
+                    const uint32_t s = g % kTcSR;
+                    if (g >= kTcSR && !mbar_wait(raw_empty(s), ((g / kTcSR) - 1) & 1, a.status)) {
+                        alive = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(raw_full(s), kTcRawBytes);
+                    tma_load_2d(sb + kTcOffRaw + s * kTcRawBytes, &tm_codes, static_cast<int32_t>(kb * (kTcBK / 2)), r0,
+                                raw_full(s));
+                }
             }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16_f32(kTcBM, kTcBN, 0, 0);
+        // ------------------------------------------------------------ MMA issuer (CTA 0, whole warp)
+        if (leader) {
+            auto wait_all = [&](uint32_t b, uint32_t parity) {  // polls with test_wait (no suspend)
+                return __all_sync(0xffffffffu, mbar_wait_spin(b, parity, a.status));
+            };
+            constexpr uint32_t idesc = idesc_bf16_f32(2 * kTcBM, 256, 0, 0);
             const uint64_t a_desc = smem_desc_sw128(sb + kTcOffA, 16, 1024);
             const uint64_t b_desc = smem_desc_sw128(sb + kTcOffB, 16, 1024);
-            for (uint32_t kb = 0; kb < nk; ++kb) {
-                const uint32_t s = kb % kTcStages, ph = (kb / kTcStages) & 1;
-                if (!mbar_wait(full_b(s), ph, a.status) || !mbar_wait(full_a(s), ph, a.status)) {
+            uint32_t g = 0, i = 0;
+            for (uint32_t t = pair; t < a.tiles && alive; t += pairs, ++i) {
+                // both CTAs' epilogues have read the previous tile's accumulator
+                if (i >= 1 && !wait_all(acc_empty, (i - 1) & 1)) {
                     alive = false;
                     break;
                 }
                 tc_fence_after();
+                for (uint32_t kb = 0; kb < nk; ++kb, ++g) {
+                    const uint32_t sbb = g % kTcSB, sa = g % kTcSA;
+                    if (!wait_all(b_full(sbb), (g / kTcSB) & 1) || !wait_all(a_full(sa), (g / kTcSA) & 1)) {
+                        alive = false;
+                        break;
+                    }
+                    tc_fence_after();
 #pragma unroll
-                for (uint32_t kk = 0; kk < kTcBK / 16; ++kk)  // K = 16 per MMA: +32 bytes inside the swizzle atom
-                    tc_mma_ss(tmem, a_desc + ((s * kTcABytes + kk * 32) >> 4), b_desc + ((s * kTcBBytes + kk * 32) >> 4),
-                              idesc, (kb | kk) ? 1u : 0u);
-                tc_commit(empty(s));
+                    for (uint32_t kk = 0; kk < kTcBK / 16; ++kk)  // K = 16 per MMA: +32 bytes inside the swizzle atom
+#pragma unroll
+                        for (uint32_t h = 0; h < 2; ++h)  // the A tile serves both 256-token halves
+                            tc_mma_ss_pair(tmem + 256 * h, a_desc + ((sa * kTcABytes + kk * 32) >> 4),
+                                           b_desc + ((sbb * kTcBBytes + h * kTcBHalf + kk * 32) >> 4), idesc,
+                                           (kb | kk) ? 1u : 0u);
+                    tc_commit_pair_both(b_empty(sbb));
+                    tc_commit_pair_both(a_empty(sa));
+                }
+                if (alive) tc_commit_pair_both(acc_full);
             }
-            if (alive) tc_commit(done);
+        }
+    } else if (warp < 2 + kTcDqWarps) {
+        // ------------------------------------------------------------ dequantise (each CTA its rows)
+        const uint32_t d = (tid - 64) >> 1, hf = tid & 1;  // row of the tile, half of its 64 weights
+        const uint32_t fa0 = mapa(a_full(0), 0);
+        uint32_t g = 0;
+        for (uint32_t t = pair; t < a.tiles && alive; t += pairs) {
+            const uint32_t grow = tile_row0(t) + d;
+            const bool row_ok = grow < a.rows;
+            const uint8_t *srow = a.scales + static_cast<uint64_t>(row_ok ? grow : 0) * (a.n / 16);
+            // the 4 scales of a 64-wide step are one aligned 32-bit word; the next step's is loaded ahead
+            uint32_t sc_next = row_ok ? __ldg(reinterpret_cast<const uint32_t *>(srow)) : 0u;
+            for (uint32_t kb = 0; kb < nk; ++kb, ++g) {
+                const uint32_t sr = g % kTcSR, s = g % kTcSA;
+                const uint32_t sc = sc_next;
+                if (kb + 1 < nk) sc_next = row_ok ? __ldg(reinterpret_cast<const uint32_t *>(srow + 4 * (kb + 1))) : 0u;
+                if (!mbar_wait(raw_full(sr), (g / kTcSR) & 1, a.status)) {
+                    alive = false;
+                    break;
+                }
+                // this thread's 32 weights: groups 2hf, 2hf + 1 of the row
+                const uint4 c = *reinterpret_cast<const uint4 *>(base + kTcOffRaw + sr * kTcRawBytes + d * (kTcBK / 2) +
+                                                                 16 * hf);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(raw_empty(sr));  // the codes are in registers
+                if (g >= kTcSA && !mbar_wait(a_empty(s), ((g / kTcSA) - 1) & 1, a.status)) {
+                    alive = false;
+                    break;
+                }
+                const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+                const uint32_t arow = sb + kTcOffA + s * kTcABytes + d * 128;  // 1024-aligned tile: row d's 128 B
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {  // 16 weights per group, its E4M3 scale
+                    const uint32_t grp = 2 * hf + q;
+                    float w[16];
+                    decode_group(make_uint2(words[2 * q], words[2 * q + 1]), w);
+                    const float scale = e4m3_to_f32(static_cast<uint8_t>((sc >> (8 * grp)) & 0xFFu));
+                    uint32_t pk[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) pk[e] = pack_bf16(w[2 * e] * scale, w[2 * e + 1] * scale);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)  // 16-byte chunk c of the row at (c ^ (row & 7)) * 16
+                        st_shared_v4(arow + (((2 * grp + h) ^ (d & 7)) << 4),
+                                     make_uint4(pk[4 * h], pk[4 * h + 1], pk[4 * h + 2], pk[4 * h + 3]));
+                }
+                // the tensor cores read the tile through the async proxy; the hand-off to CTA 0's
+                // barrier follows the proxy fence (as a TMA-written tile's completion would)
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(fa0 + 8 * s);
+            }
         }
     } else {
-        // ------------------------------------------------------------ dequantise, then epilogue
-        const uint32_t d = tid - 64;  // row of the tile this thread dequantises
-        const uint32_t grow = row0 + d;
-        const bool row_ok = grow < a.rows;
-        const uint8_t *srow = a.scales + static_cast<uint64_t>(row_ok ? grow : 0) * (a.n / 16);
-        // the 4 scales of a 64-wide step are one aligned 32-bit word; the next step's is loaded ahead
-        uint32_t sc_next = row_ok ? __ldg(reinterpret_cast<const uint32_t *>(srow)) : 0u;
-        for (uint32_t kb = 0; kb < nk; ++kb) {
-            const uint32_t s = kb % kTcStages;
-            const uint32_t sc = sc_next;
-            if (kb + 1 < nk) sc_next = row_ok ? __ldg(reinterpret_cast<const uint32_t *>(srow + 4 * (kb + 1))) : 0u;
-            if ((kb >= kTcStages && !mbar_wait(empty(s), ((kb / kTcStages) - 1) & 1, a.status)) ||
-                !mbar_wait(full_b(s), (kb / kTcStages) & 1, a.status)) {
+        // ------------------------------------------------------------ epilogue (each CTA its rows)
+        const uint32_t qd = warp & 3;  // TMEM lanes 32qd.. (this CTA's weight rows 32qd.. of the tile)
+        const uint32_t ae0 = mapa(acc_empty, 0);
+        TOut *out = static_cast<TOut *>(a.out);
+        uint32_t i = 0;
+        for (uint32_t t = pair; t < a.tiles && alive; t += pairs, ++i) {
+            if (!__all_sync(0xffffffffu, mbar_wait(acc_full, i & 1, a.status))) {
                 alive = false;
                 break;
             }
-            const uint4 *raw = reinterpret_cast<const uint4 *>(base + kTcOffRaw + s * kTcRawBytes + d * (kTcBK / 2));
-            const uint4 c0 = raw[0], c1 = raw[1];
-            const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-            const uint32_t arow = sb + kTcOffA + s * kTcABytes + d * 128;  // 1024-aligned tile: row d's 128 B
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {  // 16 weights per group, its E4M3 scale
-                float w[16];
-                decode_group(make_uint2(words[2 * g], words[2 * g + 1]), w);
-                const float scale = e4m3_to_f32(static_cast<uint8_t>((sc >> (8 * g)) & 0xFFu));
-                uint32_t pk[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) pk[i] = pack_bf16(w[2 * i] * scale, w[2 * i + 1] * scale);
-#pragma unroll
-                for (int h = 0; h < 2; ++h)  // 16-byte chunk c of the row at (c ^ (row & 7)) * 16
-                    st_shared_v4(arow + (((2 * g + h) ^ (d & 7)) << 4),
-                                 make_uint4(pk[4 * h], pk[4 * h + 1], pk[4 * h + 2], pk[4 * h + 3]));
-            }
-            fence_proxy_async_smem();  // the tensor cores read the tile through the async proxy
-            __syncwarp();
-            if (lane == 0) mbar_arrive(full_a(s));
-        }
-        if (alive && !mbar_wait(done, 0, a.status)) alive = false;
-        if (alive) {
             tc_fence_after();
-            const uint32_t q = warp & 3;  // TMEM lanes 32q.. (weight rows 32q.. of the tile)
-            const uint32_t row = row0 + 32 * q + lane;
-            const uint32_t taddr = tmem + ((32u * q) << 16);
-            TOut *out = static_cast<TOut *>(a.out);
+            const uint32_t row = tile_row0(t) + 32 * qd + lane, tok0 = tile_tok0(t);
+            const uint32_t taddr = tmem + ((32u * qd) << 16);  // column c = token tok0 + c
 #pragma unroll 1
             for (uint32_t j = 0; j < kTcBN / 32; ++j) {
                 if (tok0 + 32 * j >= a.tokens) break;  // warp-uniform
@@ -614,35 +709,72 @@ __global__ void __launch_bounds__(kTcThreads, 1) nvfp4_tc_kernel(const __grid_co
                 tmem_ld32(taddr + 32 * j, v);
                 tc_wait_ld(v);
                 if (row < a.rows) {
+                    const uint32_t n_tok = min(32u, a.tokens - (tok0 + 32 * j));
+                    TOut *dst = out + static_cast<uint64_t>(tok0 + 32 * j) * a.rows + row;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const uint32_t t = tok0 + 32 * j + i;
-                        if (t < a.tokens) store(out + static_cast<uint64_t>(t) * a.rows + row, __uint_as_float(v[i]));
+                    for (int e = 0; e < 32; ++e) {
+                        if (static_cast<uint32_t>(e) < n_tok) store(dst, __uint_as_float(v[e]));
+                        dst += a.rows;
                     }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(ae0);
         }
     }
+    // Teardown: after a failed wait copies or MMAs of the pair may still be in flight: give them time
+    // to land (bounded) before the pair releases TMEM and shared memory.
     if (!alive) err = 1;
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && err) {  // copies or MMAs may still be in flight after a failed wait
+    cluster_sync();
+    if (tid == 0 && err) {
         const long long start = clock64();
         while (clock64() - start < 400000ll) __nanosleep(1000);
     }
-    __syncthreads();
+    cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTcBN);
+        tmem_dealloc_pair(tmem, kTcBN);
     }
+}
+
+// Clusters of two that fit on the device at once with this kernel's shared memory; queried once
+// per device.
+template <typename TOut>
+uint32_t tc_max_pairs() {
+    static int cached[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && cached[dev]) return static_cast<uint32_t>(cached[dev]);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * static_cast<uint32_t>(sm_count() / 2), 1, 1);
+    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.dynamicSmemBytes = kTcSmem;
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, nvfp4_tc_kernel<TOut>, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();  // clear the query's error; fall back to one pair per two SMs
+        n = sm_count() / 2;
+    }
+    if (dev >= 0 && dev < 64) cached[dev] = n;
+    return static_cast<uint32_t>(n);
 }
 
 template <typename TOut>
 int launch_tc(const void *input, const uint32_t *codes, const uint8_t *scales, void *output, uint32_t n, uint32_t rows,
               uint32_t tokens, void *stream, const char *name) {
     CUtensorMap tx, tcodes;
-    // x [tokens][n] bf16: one box = 256 tokens x 64 elements (128-byte swizzle, K-major)
-    int rc = make_tensor_map_bf16_3d(&tx, input, n, tokens, 1, n * 2ull, n * 2ull * tokens, kTcBK, kTcBN);
+    // x [tokens][n] bf16: one box = 128 tokens x 64 elements (128-byte swizzle, K-major): a CTA's
+    // share of one N = 256 MMA
+    int rc = make_tensor_map_bf16_3d(&tx, input, n, tokens, 1, n * 2ull, n * 2ull * tokens, kTcBK, 128);
     if (rc) return rc;
     // codes [rows][n/2] bytes: one box = 128 rows x 32 bytes (64 weights)
     rc = make_tensor_map_u8_2d(&tcodes, codes, n / 2, rows, n / 2, kTcBK / 2, kTcBM);
@@ -665,7 +797,9 @@ int launch_tc(const void *input, const uint32_t *codes, const uint8_t *scales, v
     ta.rows = rows;
     ta.n = n;
     ta.tokens = tokens;
-    const dim3 grid((rows + kTcBM - 1) / kTcBM, (tokens + kTcBN - 1) / kTcBN);
+    ta.tiles_n = (tokens + kTcBN - 1) / kTcBN;
+    ta.tiles = ((rows + 2 * kTcBM - 1) / (2 * kTcBM)) * ta.tiles_n;
+    const uint32_t grid = 2 * std::min<uint32_t>(ta.tiles, tc_max_pairs<TOut>());  // one CTA pair per two SMs
     nvfp4_tc_kernel<TOut><<<grid, kTcThreads, kTcSmem, static_cast<cudaStream_t>(stream)>>>(tx, tcodes, ta);
     rc = check_cuda(cudaGetLastError(), name);
     return rc ? rc : ok();
@@ -675,7 +809,8 @@ int launch_tc(const void *input, const uint32_t *codes, const uint8_t *scales, v
 // 16-byte aligned input and codes and 4-byte aligned scales.
 bool tc_applies(bool in_bf16, const void *input, const uint32_t *codes, const uint8_t *scales, uint32_t n,
                 uint32_t tokens, uint32_t rows) {
-    return in_bf16 && tokens >= kTcMinTokens && n % kTcBK == 0 && rows > 0 && tokens <= 65535u * kTcBN &&
+    return in_bf16 && tokens >= kTcMinTokens && n % kTcBK == 0 && rows > 0 &&
+           static_cast<uint64_t>((rows + kTcBM - 1) / kTcBM) * ((tokens + kTcBN - 1) / kTcBN) < (1ull << 31) &&
            !(reinterpret_cast<uintptr_t>(input) & 15) && !(reinterpret_cast<uintptr_t>(codes) & 15) &&
            !(reinterpret_cast<uintptr_t>(scales) & 3);
 }
