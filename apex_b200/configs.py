@@ -72,6 +72,10 @@ CONFIGS = {
         "global_decode", "decode", batch=8, seed=11, rope_theta=1e6, context=32768, q_heads=16, kv_heads=2,
         head_dim=512, v_norm=True, partial_rope=64,
         note="global-layer decode: 8 x 32768 keys, 2 kv heads of 512, GQA group 8"),
+    "global_prefill": AttnConfig(
+        "global_prefill", "prefill", batch=1, seed=12, rope_theta=1e6, seq_len=4096, chunk=4096, q_heads=16,
+        kv_heads=2, head_dim=512, v_norm=True, partial_rope=64,
+        note="global-layer prefill: one 4096-token chunk, 2 kv heads of 512, GQA group 8, global causal"),
     # not an attention configuration: the NVFP4 projections either side of one decode step
     "proj_decode": AttnConfig(
         "proj_decode", "proj", batch=1, seed=9, rope_theta=1e4,

@@ -224,6 +224,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
         : "memory");
 }
+// 4-D tiled load global -> shared (this CTA), completing on `bar`; no multicast.  c0 * element size
+// must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int32_t c0, int32_t c1, int32_t c2,
+                                            int32_t c3, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+        : "memory");
+}
 // 4-D tiled store shared -> global (bulk async group; no multicast).  Elements outside the
 // tensor are not written.  c0 * element size must be a multiple of 16 bytes.
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, uint32_t src, int32_t c0, int32_t c1, int32_t c2,

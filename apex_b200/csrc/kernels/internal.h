@@ -60,4 +60,16 @@ int launch_gqa_decode(const apex_attn_params *p, const uint16_t *q_raw, const ui
                       uint32_t capacity, const int32_t *seq_lens, uint32_t batch, uint32_t max_seq_len,
                       uint16_t *out, void *workspace, size_t workspace_bytes_given, void *stream, const char *name);
 
+// Prefill for head_dim 512 (prefill_gqa.cu), arguments validated by the caller: the q workspace
+// [B][Hq][T][512] it needs, the preparation (q into the workspace; k and v into the caches at pos0)
+// and the attention over the caches.
+size_t prefill_gqa_workspace_bytes(uint32_t batch, uint32_t tokens, uint32_t q_heads);
+int launch_prefill_gqa_prep(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t *k_raw,
+                            const uint16_t *v_raw, const uint16_t *q_w, const uint16_t *k_w, uint16_t *k_cache,
+                            uint16_t *v_cache, uint32_t capacity, uint32_t batch, uint32_t tokens, uint32_t pos0,
+                            void *workspace, cudaStream_t s);
+int launch_prefill_gqa_attend(const apex_attn_params *p, const void *workspace, const uint16_t *k_cache,
+                              const uint16_t *v_cache, uint32_t capacity, uint32_t batch, uint32_t tokens,
+                              uint32_t pos0, uint16_t *out, cudaStream_t s);
+
 }  // namespace apex

@@ -895,6 +895,13 @@ size_t ws_bytes(uint32_t batch, uint32_t tokens, uint32_t q_heads) {
     return align256(q_ws_bytes(batch, tokens, q_heads)) + 256;  // + scheduler counters
 }
 
+constexpr uint32_t kWideD = 512;  // the global layers' head_dim (prefill_gqa.cu)
+
+size_t ws_bytes_for(const apex_attn_params *p, uint32_t batch, uint32_t tokens) {
+    return p->head_dim == kWideD ? prefill_gqa_workspace_bytes(batch, tokens, p->q_heads)
+                                 : ws_bytes(batch, tokens, p->q_heads);
+}
+
 unsigned *sched_ptr(void *workspace, uint32_t batch, uint32_t tokens, uint32_t q_heads) {
     return reinterpret_cast<unsigned *>(static_cast<uint8_t *>(workspace) +
                                         align256(q_ws_bytes(batch, tokens, q_heads)));
@@ -905,11 +912,14 @@ int validate_prefill(const apex_attn_params *p, uint32_t capacity, uint32_t batc
                      size_t workspace_bytes, const char *name) {
     const std::string n(name);
     if (!p) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": null params");
-    if (p->head_dim != kD) return fail(APEX_ERR_UNSUPPORTED, n + ": this build supports head_dim 256");
+    const bool wide = p->head_dim == kWideD;
+    if (p->head_dim != kD && !wide) return fail(APEX_ERR_UNSUPPORTED, n + ": this build supports head_dim 256 and 512");
+    if (wide && !p->qk_norm)
+        return fail(APEX_ERR_UNSUPPORTED, n + ": head_dim 512 prefill normalises q and k (qk_norm = 1)");
     if (p->ring) return fail(APEX_ERR_UNSUPPORTED, n + ": prefill writes a linear cache (copy its last keys into a ring with apex_kv_ring_store)");
     if (p->kv_heads == 0 || p->q_heads == 0 || p->q_heads % p->kv_heads)
         return fail(APEX_ERR_INVALID_ARGUMENT, n + ": q_heads must be a multiple of kv_heads");
-    if (p->rope_pairs > kD / 2) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": rope_pairs > head_dim / 2");
+    if (p->rope_pairs > p->head_dim / 2) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": rope_pairs > head_dim / 2");
     if (batch == 0 || tokens == 0) return APEX_OK;
     for (const void *ptr : tensors) {
         if (!ptr) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": null tensor");
@@ -917,13 +927,22 @@ int validate_prefill(const apex_attn_params *p, uint32_t capacity, uint32_t batc
     }
     if (static_cast<uint64_t>(pos0) + tokens > capacity)
         return fail(APEX_ERR_INVALID_ARGUMENT, n + ": pos0 + tokens exceeds capacity");
-    const uint64_t items = static_cast<uint64_t>(batch) * p->q_heads * ((tokens + kBM - 1) / kBM);
-    if (items > 0x7fffffffull) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": problem too large for one launch");
+    if (wide) {
+        // grid (ceil(T / 16) x kv heads x ceil(group / 2), 1, batch); the norm-and-RoPE launches take
+        // strides of tokens x 512 and capacity x 512 elements as 32-bit values
+        const uint64_t gx = static_cast<uint64_t>(p->kv_heads) * ((p->q_heads / p->kv_heads + 1) / 2) *
+                            ((tokens + 15) / 16);
+        if (gx > 0x7fffffffull || batch > 65535 || static_cast<uint64_t>(capacity) * kWideD > 0xffffffffull)
+            return fail(APEX_ERR_INVALID_ARGUMENT, n + ": problem too large for one launch");
+    } else {
+        const uint64_t items = static_cast<uint64_t>(batch) * p->q_heads * ((tokens + kBM - 1) / kBM);
+        if (items > 0x7fffffffull) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": problem too large for one launch");
+        if (p->q_heads + 2 * p->kv_heads > kPrepMaxRows)
+            return fail(APEX_ERR_UNSUPPORTED, n + ": more than 96 q + k + v heads per token");
+    }
     if (static_cast<uint64_t>(batch) * tokens > 0xffffffffull)
         return fail(APEX_ERR_INVALID_ARGUMENT, n + ": problem too large for one launch");
-    if (p->q_heads + 2 * p->kv_heads > kPrepMaxRows)
-        return fail(APEX_ERR_UNSUPPORTED, n + ": more than 96 q + k + v heads per token");
-    const size_t need = ws_bytes(batch, tokens, p->q_heads);
+    const size_t need = ws_bytes_for(p, batch, tokens);
     if (!workspace || workspace_bytes < need)
         return fail(APEX_ERR_WORKSPACE, n + ": workspace of " + std::to_string(need) + " bytes required");
     if (!aligned16(workspace)) return fail(APEX_ERR_INVALID_ARGUMENT, n + ": tensors must be 16-byte aligned");
@@ -1063,7 +1082,7 @@ int launch_attend(const apex_attn_params *p, void *workspace, const uint16_t *k_
 extern "C" size_t apex_attn_prefill_workspace_bytes(const apex_attn_params *p, uint32_t batch,
                                                     uint32_t tokens) {
     if (!p) return 0;
-    return apex::ws_bytes(batch, tokens, p->q_heads);
+    return apex::ws_bytes_for(p, batch, tokens);
 }
 
 extern "C" int apex_attn_prefill_prep_bf16(const apex_attn_params *p, const uint16_t *q_raw,
@@ -1076,8 +1095,11 @@ extern "C" int apex_attn_prefill_prep_bf16(const apex_attn_params *p, const uint
     int rc = validate_prefill(p, capacity, batch, tokens, pos0, {q_raw, k_raw, v_raw, k_cache, v_cache}, workspace,
                               workspace_bytes, "apex_attn_prefill_prep_bf16");
     if (rc || batch == 0 || tokens == 0) return rc ? rc : ok();
-    rc = launch_prep(p, q_raw, k_raw, v_raw, q_norm_w, k_norm_w, k_cache, v_cache, capacity, batch, tokens, pos0,
-                     workspace, static_cast<cudaStream_t>(stream));
+    rc = p->head_dim == kWideD
+             ? launch_prefill_gqa_prep(p, q_raw, k_raw, v_raw, q_norm_w, k_norm_w, k_cache, v_cache, capacity, batch,
+                                       tokens, pos0, workspace, static_cast<cudaStream_t>(stream))
+             : launch_prep(p, q_raw, k_raw, v_raw, q_norm_w, k_norm_w, k_cache, v_cache, capacity, batch, tokens,
+                           pos0, workspace, static_cast<cudaStream_t>(stream));
     return rc ? rc : ok();
 }
 
@@ -1090,8 +1112,11 @@ extern "C" int apex_attn_prefill_attend_bf16(const apex_attn_params *p, void *wo
     int rc = validate_prefill(p, capacity, batch, tokens, pos0, {k_cache, v_cache, out}, workspace, workspace_bytes,
                               "apex_attn_prefill_attend_bf16");
     if (rc || batch == 0 || tokens == 0) return rc ? rc : ok();
-    rc = launch_attend(p, workspace, k_cache, v_cache, capacity, batch, tokens, pos0, out,
-                       static_cast<cudaStream_t>(stream));
+    rc = p->head_dim == kWideD
+             ? launch_prefill_gqa_attend(p, workspace, k_cache, v_cache, capacity, batch, tokens, pos0, out,
+                                         static_cast<cudaStream_t>(stream))
+             : launch_attend(p, workspace, k_cache, v_cache, capacity, batch, tokens, pos0, out,
+                             static_cast<cudaStream_t>(stream));
     return rc ? rc : ok();
 }
 
@@ -1107,6 +1132,13 @@ extern "C" int apex_attn_prefill_bf16(const apex_attn_params *p, const uint16_t 
                               workspace, workspace_bytes, "apex_attn_prefill_bf16");
     if (rc || batch == 0 || tokens == 0) return rc ? rc : ok();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (p->head_dim == kWideD) {
+        rc = launch_prefill_gqa_prep(p, q_raw, k_raw, v_raw, q_norm_w, k_norm_w, k_cache, v_cache, capacity, batch,
+                                     tokens, pos0, workspace, s);
+        if (rc) return rc;
+        rc = launch_prefill_gqa_attend(p, workspace, k_cache, v_cache, capacity, batch, tokens, pos0, out, s);
+        return rc ? rc : ok();
+    }
     rc = launch_prep(p, q_raw, k_raw, v_raw, q_norm_w, k_norm_w, k_cache, v_cache, capacity, batch, tokens, pos0,
                      workspace, s);
     if (rc) return rc;

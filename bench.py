@@ -15,8 +15,9 @@ fields): c1_decode, c2_prefill_window (one fused prefill = prep + tcgen05 attent
 c3_ragged_decode, c4_chunked_prefill (one step = the whole 32768-token prefill of 4 sequences in
 8 chunks of 4096 appended to the cache in order), c5_long_decode_b1, global_decode (the reference
 model's global layers: 8 decodes over 32768 keys of 2 kv heads of head_dim 512, GQA group 8, RoPE on
-64 pairs, V norm) and proj_decode (the NVFP4 q/k/v projections and o_proj + post-attention RMSNorm of
-one decode token).  At N > 1: c1 / c2 / proj run replicas (weak scaling); c3 and global_decode shard
+64 pairs, V norm), global_prefill (the same layers' prefill of one 4096-token chunk) and proj_decode /
+proj_prefill (the NVFP4 q/k/v projections and o_proj + post-attention RMSNorm of one decode token /
+one 4096-token chunk).  At N > 1: c1 / c2 / global_prefill / proj run replicas (weak scaling); c3 and global_decode shard
 sequences; c4 shards sequences where the batch divides over the GPUs and kv heads otherwise; c5 splits
 the KV sequence (strong scaling).
 
@@ -57,7 +58,7 @@ from apex_b200.configs import CONFIGS, decode_bytes, prefill_flops, visible_pair
 
 PRIMARY = "c5_long_decode_b8"
 ALSO = ("c1_decode", "c2_prefill_window", "c3_ragged_decode", "c4_chunked_prefill", "c5_long_decode_b1",
-        "global_decode", "proj_decode", "proj_prefill")
+        "global_decode", "global_prefill", "proj_decode", "proj_prefill")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_BYTES = 126 * 1024 * 1024
 TOL_MAX, TOL_MEAN = 2e-2, 2e-3          # against an fp32 reference
@@ -238,7 +239,8 @@ class PrefillWorkload:
         owns_tokens = self.sharding != "kv-head-shard" or rank == 0
         self.tokens = B * T * C if owns_tokens else 0
         self.launches_per_step = 2 * C
-        self.kernel_name = "prefill_pair_kernel"
+        # head_dim 512 (the global layers) runs the mma.sync form of prefill_gqa.cu
+        self.kernel_name = "prefill_gqa_kernel" if cfg.head_dim == 512 else "prefill_pair_kernel"
 
     def _chunk(self, s, c, out, ws):
         self.ops.attention_prefill_prep(self.shape, s["q"][c], s["k"][c], s["v"][c], self.qw, self.kw, s["cache"],
@@ -630,7 +632,11 @@ def _ref_decode_setup(cfg, b, L, ref):
     del k
     v = I.f32(I.v_rows(cfg, b, 0, L))
     Vc = np.zeros(Hkv * L * D, np.float32)
-    Vc.reshape(Hkv, L, D)[:, :L - 1] = v[:L - 1].transpose(1, 0, 2)
+    if cfg.v_norm:  # the global layers: weightless RMSNorm of V (docs/B6_3_attention.md:25)
+        oracle.head_norm_rope_f32(v[:L - 1], None, Vc, L - 1, Hkv, D, 0, 0, cfg.rope_theta, 0, D, L * D, cfg.eps,
+                                  ref=ref)
+    else:
+        Vc.reshape(Hkv, L, D)[:, :L - 1] = v[:L - 1].transpose(1, 0, 2)
     new = (I.f32(I.q_rows(cfg, b, L - 1, L)), I.f32(I.k_rows(cfg, b, L - 1, L)), v[L - 1:].copy())
     _REF_CACHE[key] = (Kc, Vc, new, qw, kw)
     return _REF_CACHE[key]
@@ -670,11 +676,11 @@ def cpu_reference_step(cfg, threads):
         return dt, nbytes, "the four projections of one decode token (matvecNvfp4Cpu) + rmsNormCpu; value = weight bytes / time", kind
     Hq, Hkv, D = cfg.q_heads, cfg.kv_heads, cfg.head_dim
     if cfg.kind == "prefill":
-        # c2: the whole prompt; c4: 16 query rows of the last chunk of sequence 0 (the cache of the
-        # earlier chunks is built outside the timed region)
+        # c2: the whole prompt; c4 and global_prefill: 16 query rows of the last chunk of sequence 0
+        # (the cache of the earlier chunks is built outside the timed region)
         qw, kw = I.norm_weights(cfg)
         S = cfg.seq_len
-        last = cfg.name.startswith("c4")
+        last = cfg.name.startswith("c4") or cfg.head_dim == 512
         key = (cfg.name, "prefill")
         if key not in _REF_CACHE:
             _REF_CACHE[key] = (I.f32(I.q_rows(cfg, 0, 0, S)).ravel(), I.f32(I.k_rows(cfg, 0, 0, S)),
@@ -693,7 +699,11 @@ def cpu_reference_step(cfg, threads):
             t0 = time.perf_counter()
             oracle.head_norm_rope_f32(k[p0:], kw, Kc[p0 * D:], S - p0, Hkv, D, 1, cfg.rope_pairs, cfg.rope_theta, p0, D,
                                       S * D, cfg.eps, ref=ref)
-            Vc = np.ascontiguousarray(v.transpose(1, 0, 2)).ravel()
+            if cfg.v_norm:
+                Vc = np.zeros(Hkv * S * D, np.float32)
+                oracle.head_norm_rope_f32(v, None, Vc, S, Hkv, D, 0, 0, cfg.rope_theta, 0, D, S * D, cfg.eps, ref=ref)
+            else:
+                Vc = np.ascontiguousarray(v.transpose(1, 0, 2)).ravel()
             qs = np.ascontiguousarray(q_all.reshape(S, Hq, D)[rows]).ravel()
             qn = np.zeros_like(qs)
             for i, r in enumerate(rows):
@@ -705,7 +715,8 @@ def cpu_reference_step(cfg, threads):
             dt = time.perf_counter() - t0
             flops = 4 * Hq * D * sum(visible_pairs(r, 1, cfg.window) for r in rows)
             desc = (f"{len(rows)} query rows of the last chunk (positions {rows[0]}..{rows[-1]}) x {Hq} heads of "
-                    f"sequence 0, with that chunk's K/V norm + RoPE into the cache; value = the sample's FLOPs / time")
+                    f"sequence 0, with that chunk's K norm + RoPE{' and V norm' if cfg.v_norm else ''} into the "
+                    f"cache; value = the sample's FLOPs / time")
             return dt, flops, desc, kind
         t0 = time.perf_counter()
         Kc = np.zeros(Hkv * S * D, np.float32)
@@ -731,7 +742,11 @@ def cpu_reference_step(cfg, threads):
                                   ref=ref)
         oracle.head_norm_rope_f32(kn, kw, Kc[(L - 1) * D:], 1, Hkv, D, 1, cfg.rope_pairs, cfg.rope_theta, L - 1, D,
                                   L * D, cfg.eps, ref=ref)
-        Vc.reshape(Hkv, L, D)[:, L - 1] = vn[0]
+        if cfg.v_norm:
+            oracle.head_norm_rope_f32(vn, None, Vc[(L - 1) * D:], 1, Hkv, D, 0, 0, cfg.rope_theta, L - 1, D, L * D,
+                                      cfg.eps, ref=ref)
+        else:
+            Vc.reshape(Hkv, L, D)[:, L - 1] = vn[0]
         oracle.attention_f32(qn, Kc, Vc, 1, Hq, Hkv, D, L, L - 1, cfg.window, cfg.scale, ref=ref)
     dt = time.perf_counter() - t0
     nbytes = decode_bytes(cfg, [lens[b] for b in seqs])

@@ -50,6 +50,9 @@ def test_workspace_sizes_are_host_computable():
     p = _params()
     # normalised q (bf16, head-major) + 256 bytes of scheduler state
     assert lib.apex_attn_prefill_workspace_bytes(ctypes.byref(p), 1, 2048) == 2048 * 16 * 256 * 2 + 256
+    # head_dim 512 (the global layers): the normalised q alone
+    g = _params(q_heads=16, kv_heads=2, head_dim=512, rope_pairs=64)
+    assert lib.apex_attn_prefill_workspace_bytes(ctypes.byref(g), 2, 1000) == 2 * 16 * 1000 * 512 * 2
     small = lib.apex_attn_decode_workspace_bytes(ctypes.byref(p), 1, 1024)
     big = lib.apex_attn_decode_workspace_bytes(ctypes.byref(p), 64, 8192)
     assert 0 < small < big
@@ -57,7 +60,9 @@ def test_workspace_sizes_are_host_computable():
 
 @pytest.mark.parametrize("kw,code", [(dict(head_dim=128), _native.APEX_ERR_UNSUPPORTED),
                                      (dict(q_heads=12, kv_heads=8), _native.APEX_ERR_INVALID_ARGUMENT),
-                                     (dict(rope_pairs=200), _native.APEX_ERR_INVALID_ARGUMENT)])
+                                     (dict(rope_pairs=200), _native.APEX_ERR_INVALID_ARGUMENT),
+                                     (dict(head_dim=512, rope_pairs=300), _native.APEX_ERR_INVALID_ARGUMENT),
+                                     (dict(head_dim=512, rope_pairs=64, qk_norm=0), _native.APEX_ERR_UNSUPPORTED)])
 def test_prefill_rejects_bad_params_without_gpu(kw, code):
     lib = _native.load()
     p = _params(**kw)
