@@ -40,7 +40,8 @@ constexpr int kStagePos = 16;      // keys per stage (MMA M)
 constexpr int kWarps = 4;          // consumer warps
 constexpr int kThreads = (kWarps + 1) * 32;
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr uint32_t kMaxSplits = 4096;  // the last CTA's merge keeps kHeads x splits weights in the ring
+constexpr uint32_t kMaxSplits = 4096;
+constexpr uint32_t kGroup = 8;         // splits merged by the last CTA of each group
 
 struct GqaArgs {
     const uint16_t *q_raw, *k_new, *v_new, *q_w, *k_w;
@@ -48,17 +49,17 @@ struct GqaArgs {
     const int32_t *seq_lens;
     uint16_t *out;
     float *ws_part;      // [B][Hq][max_splits][D + 4]
-    unsigned *ws_count;  // [B][Hkv]
+    unsigned *ws_count;  // [B][Hkv] splits (or groups of splits) done
+    unsigned *ws_gcount; // [B][Hkv][max_groups] splits of each group done
     unsigned *status;
     uint32_t capacity, q_heads, kv_heads, group, rope_pairs, window, qk_norm, v_norm;
-    uint32_t chunk, max_splits, max_seq_len;
+    uint32_t chunk, max_splits, max_groups, max_seq_len;
     float eps, scale_log2;
     RopeTable rope;
 };
 
 template <int D>
 struct GqaSmem {
-    static constexpr int kChunks = D / 64;                      // 128-byte chunks of a row
     static constexpr int kTile = kStagePos * D * 2;             // one operand's 16 keys, swizzled
     static constexpr int kStageBytes = 2 * kTile;               // K tile then V tile
     static constexpr int kStages = D == 512 ? 4 : 8;            // 128 KB of K/V in flight
@@ -70,9 +71,15 @@ struct GqaSmem {
     uint64_t full[kStages], empty[kStages];
     int is_last;
 };
-static_assert(sizeof(GqaSmem<256>::ring) >= kHeads * kMaxSplits * sizeof(float) &&
-                  sizeof(GqaSmem<512>::ring) >= kHeads * kMaxSplits * sizeof(float),
-              "merge weights fit in the ring");
+// The merges stage up to kHeads x (kGroup + 1) partial records at once in the ring and the tail
+// (contiguous), and keep the batch's weights beside them in q's space.
+static_assert(offsetof(GqaSmem<512>, tail) == sizeof(GqaSmem<512>::ring) &&
+                  offsetof(GqaSmem<256>, tail) == sizeof(GqaSmem<256>::ring),
+              "ring and tail are one staging area");
+static_assert(sizeof(GqaSmem<512>::ring) + sizeof(GqaSmem<512>::tail) >= kHeads * (kGroup + 1) * (512 + 4) * 4 &&
+                  sizeof(GqaSmem<256>::ring) + sizeof(GqaSmem<256>::tail) >= kHeads * (kGroup + 1) * (256 + 4) * 4,
+              "a batch of partial records fits the staging area");
+static_assert(sizeof(GqaSmem<256>::q) >= kHeads * (kGroup + 1 + 2) * 4, "batch weights fit q's space");
 
 __device__ __forceinline__ void gqa_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWarps * 32) : "memory"); }
 
@@ -130,7 +137,7 @@ __device__ __forceinline__ uint32_t tile_off(uint32_t key, uint32_t col) {
 template <int D>
 __device__ __forceinline__ void gqa_tile(uint32_t kbase, uint32_t vbase, int nvalid, uint32_t lane, uint32_t qhi,
                                          uint32_t qlo, float (&m)[2], float (&l)[2], float (&o)[D / 16][4]) {
-    const uint32_t g = lane >> 2, c = lane & 3;
+    const uint32_t g = lane >> 2;
     const uint32_t mi = lane >> 3, r = lane & 7;
     // A = K keys: matrix mi covers keys r + 8*(mi & 1), the 16-byte column 2*kk + (mi >> 1) of step kk
     const uint32_t a_key = r + 8 * (mi & 1), a_col = mi >> 1;
@@ -200,6 +207,113 @@ __device__ __forceinline__ void gqa_tile(uint32_t kbase, uint32_t vbase, int nva
         uint32_t a[4];
         ldsm_x4_t(vbase + tile_off(v_key, 2 * t + v_col), a);
         mma_bf16(o[t], a, b0, b1);
+    }
+}
+
+// Merges n partial records of every head -- head h's record i at part + ((rows_b + h) * max_splits +
+// first + i * stride) * (D + 4): o normalised by its l, then m (log2 units) and l -- staged kGroup + 1
+// at a time in the ring and tail by cp.async (one round trip per batch), with the running max and
+// weight sum of each head rescaled from batch to batch.  final_out: o / sum to bf16 out; otherwise
+// the merged record (o normalised, m, l = the weight sum) replaces record `first`.  Thread t owns
+// float4 column t % (D/4) of heads t / (D/4), + 128 / (D/4), ...
+template <int D>
+__device__ void merge_records(GqaSmem<D> &sm, const GqaArgs &a, float *part, uint64_t rows_b, uint32_t G,
+                              uint32_t first, uint32_t stride, uint32_t n, bool final_out, uint32_t tid) {
+    constexpr uint32_t kRec = D + 4;
+    constexpr uint32_t kCols = D / 4;
+    constexpr uint32_t kHStep = kWarps * 32 / kCols;
+    constexpr uint32_t kHpt = kHeads / kHStep;
+    constexpr uint32_t kBatch = kGroup + 1;
+    const uint32_t warp = tid >> 5, lane = tid & 31;
+    const uint32_t col = tid % kCols, h0 = tid / kCols;
+    float *stage = reinterpret_cast<float *>(sm.ring[0]);    // [head][kBatch][kRec]
+    float *wts = reinterpret_cast<float *>(&sm.q[0][0][0]);  // [head][kBatch]
+    float *scl = wts + kHeads * kBatch;                      // [head] rescale of the running sums
+    float *den = scl + kHeads;                               // [head] running weight sum
+    float *mrun = den + kHeads;                              // [head] running max
+    float acc[kHpt][4];
+#pragma unroll
+    for (uint32_t k = 0; k < kHpt; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.f;
+    if (tid < kHeads) {
+        den[tid] = 0.f;
+        mrun[tid] = -INFINITY;
+    }
+    for (uint32_t i0 = 0; i0 < n; i0 += kBatch) {
+        const uint32_t cnt = min(kBatch, n - i0);
+        const uint32_t per_h = cnt * (kRec / 4);  // 16-byte pieces of one head's records
+        for (uint32_t q = tid; q < G * per_h; q += kWarps * 32) {
+            const uint32_t h = q / per_h, rem = q % per_h, i = rem / (kRec / 4), w16 = rem % (kRec / 4);
+            const float *src = part + ((rows_b + h) * a.max_splits + first + (i0 + i) * stride) * kRec + 4 * w16;
+            cp_async16(smem_u32(stage + (h * kBatch + i) * kRec + 4 * w16), src);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        gqa_sync();
+        for (uint32_t h = warp; h < G; h += kWarps) {  // weights of the batch; lane i: record i
+            const bool has = lane < cnt;
+            const float *rec = stage + (h * kBatch + (has ? lane : 0)) * kRec;
+            const float mi = has ? rec[D] : -INFINITY, li = has ? rec[D + 1] : 0.f;
+            float M = li > 0.f ? mi : -INFINITY;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+            const float m_old = mrun[h];
+            const float Mn = fmaxf(m_old, M);
+            const float wt = li > 0.f ? fast_exp2(mi - Mn) * li : 0.f;
+            float sum = wt;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            if (has) wts[h * kBatch + lane] = wt;
+            __syncwarp();
+            if (lane == 0) {
+                const float sc = m_old == -INFINITY ? 0.f : fast_exp2(m_old - Mn);
+                scl[h] = sc;
+                den[h] = den[h] * sc + sum;
+                mrun[h] = Mn;
+            }
+        }
+        gqa_sync();
+#pragma unroll
+        for (uint32_t k = 0; k < kHpt; ++k) {
+            const uint32_t h = h0 + k * kHStep;
+            if (h >= G) continue;
+            const float sc = scl[h];
+            float r[4] = {acc[k][0] * sc, acc[k][1] * sc, acc[k][2] * sc, acc[k][3] * sc};
+            const float *srec = stage + h * kBatch * kRec + 4 * col;
+            for (uint32_t i = 0; i < cnt; ++i) {
+                const float wt = wts[h * kBatch + i];
+                const float4 v = *reinterpret_cast<const float4 *>(srec + i * kRec);
+                r[0] += wt * v.x;
+                r[1] += wt * v.y;
+                r[2] += wt * v.z;
+                r[3] += wt * v.w;
+            }
+            acc[k][0] = r[0];
+            acc[k][1] = r[1];
+            acc[k][2] = r[2];
+            acc[k][3] = r[3];
+        }
+        gqa_sync();  // the staging area is free for the next batch
+    }
+#pragma unroll
+    for (uint32_t k = 0; k < kHpt; ++k) {
+        const uint32_t h = h0 + k * kHStep;
+        if (h >= G) continue;
+        const float dn = den[h];
+        const float inv = dn > 0.f ? 1.0f / dn : 0.f;
+        if (final_out) {
+            uint2 pk;
+            pk.x = pack_bf16(acc[k][0] * inv, acc[k][1] * inv);
+            pk.y = pack_bf16(acc[k][2] * inv, acc[k][3] * inv);
+            *reinterpret_cast<uint2 *>(a.out + (rows_b + h) * D + 4 * col) = pk;
+        } else {
+            float *dst = part + ((rows_b + h) * a.max_splits + first) * kRec;
+            *reinterpret_cast<float4 *>(dst + 4 * col) =
+                make_float4(acc[k][0] * inv, acc[k][1] * inv, acc[k][2] * inv, acc[k][3] * inv);
+            if (col == 0) {
+                dst[D] = mrun[h];
+                dst[D + 1] = dn;
+            }
+        }
     }
 }
 
@@ -401,79 +515,43 @@ __global__ void __launch_bounds__(kThreads, 1) decode_gqa_kernel(const __grid_co
         }
     }
     if (nsplit == 1) return;
+    // ---- splits in groups of kGroup: the last CTA of a group merges the group into the group's first
+    // record, and the last group's merger merges the groups into out (one level for <= kGroup splits).
+    // Each merger stages its records by cp.async in one or a few round trips, so no single CTA reads
+    // hundreds of partials one load at a time.
+    const uint32_t ngroups = (nsplit + kGroup - 1) / kGroup;
+    if (ngroups > 1) {
+        const uint32_t grp = split / kGroup, gsize = min(kGroup, nsplit - grp * kGroup);
+        gqa_sync();
+        if (tid == 0) {
+            __threadfence();
+            unsigned *gc = a.ws_gcount + (static_cast<uint64_t>(b) * a.kv_heads + kvh) * a.max_groups + grp;
+            const unsigned prev = atomicAdd(gc, 1u);
+            const int last = prev == gsize - 1;
+            if (last) *gc = 0;
+            sm.is_last = last;
+        }
+        gqa_sync();
+        if (!sm.is_last) return;
+        __threadfence();
+        if (gsize > 1) merge_records<D>(sm, a, part, rows_b, G, grp * kGroup, 1, gsize, false, tid);
+    }
     gqa_sync();
     if (tid == 0) {
         __threadfence();
         unsigned *counter = a.ws_count + static_cast<uint64_t>(b) * a.kv_heads + kvh;
         const unsigned prev = atomicAdd(counter, 1u);
-        const int last = prev == nsplit - 1;
+        const int last = prev == (ngroups > 1 ? ngroups : nsplit) - 1;
         if (last) *counter = 0;
         sm.is_last = last;
     }
     gqa_sync();
     if (!sm.is_last) return;
     __threadfence();
-    // ---- last CTA: merge the nsplit partials of every head.  Warp w takes heads w, w + 4: the max
-    // of the splits' m, then their weights 2^(m - M) l into shared memory (the ring is free) and the
-    // weights' sum; then every thread accumulates its 4-dim chunks over the splits, eight
-    // independent 16-byte loads in flight.
-    float *wts = reinterpret_cast<float *>(sm.ring[0]);  // [G][nsplit]: G * nsplit * 4 <= 128 KB
-    float *den_h = sm.red_l[0];                          // [G] sums of the weights
-    for (uint32_t h = warp; h < G; h += kWarps) {
-        const float *base = part + (rows_b + h) * a.max_splits * (D + 4);
-        float M = -INFINITY;
-        for (uint32_t sp = lane; sp < nsplit; sp += 32) {
-            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(base + sp * (D + 4) + D));
-            if (ml.y > 0.f) M = fmaxf(M, ml.x);
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-        float den = 0.f;
-        for (uint32_t sp = lane; sp < nsplit; sp += 32) {
-            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(base + sp * (D + 4) + D));
-            const float wt = ml.y > 0.f ? fast_exp2(ml.x - M) * ml.y : 0.f;
-            wts[h * nsplit + sp] = wt;
-            den += wt;
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
-        if (lane == 0) den_h[h] = den;
-    }
-    gqa_sync();
-    for (uint32_t ch = tid; ch < G * (D / 4); ch += kWarps * 32) {
-        const uint32_t h = ch / (D / 4), d0 = (ch % (D / 4)) * 4;
-        const float *pg = part + (rows_b + h) * a.max_splits * (D + 4) + d0;
-        const float *wg = wts + h * nsplit;
-        float r4[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t sp = 0;
-        for (; sp + 8 <= nsplit; sp += 8) {
-            float4 v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = __ldcg(reinterpret_cast<const float4 *>(pg + (sp + u) * (D + 4)));
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const float wt = wg[sp + u];
-                r4[0] += wt * v[u].x;
-                r4[1] += wt * v[u].y;
-                r4[2] += wt * v[u].z;
-                r4[3] += wt * v[u].w;
-            }
-        }
-        for (; sp < nsplit; ++sp) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(pg + sp * (D + 4)));
-            const float wt = wg[sp];
-            r4[0] += wt * v.x;
-            r4[1] += wt * v.y;
-            r4[2] += wt * v.z;
-            r4[3] += wt * v.w;
-        }
-        const float den = den_h[h];
-        const float inv = den > 0.f ? 1.0f / den : 0.f;
-        uint2 pk;
-        pk.x = pack_bf16(r4[0] * inv, r4[1] * inv);
-        pk.y = pack_bf16(r4[2] * inv, r4[3] * inv);
-        *reinterpret_cast<uint2 *>(a.out + (rows_b + h) * D + d0) = pk;
-    }
+    if (ngroups > 1)
+        merge_records<D>(sm, a, part, rows_b, G, 0, kGroup, ngroups, true, tid);
+    else
+        merge_records<D>(sm, a, part, rows_b, G, 0, 1, nsplit, true, tid);
 }
 
 uint32_t gqa_max_splits(uint32_t batch, uint32_t kv_heads, uint32_t max_len) {
@@ -507,10 +585,14 @@ bool gqa_decode_form(const apex_attn_params *p) {
     return (p->head_dim == 256 || p->head_dim == 512) && g >= 1 && g <= kHeads;
 }
 
+// Workspace: partial records [B][Hq][max_splits][D + 4] f32, then the counters: [B][Hkv] splits or
+// groups done, then [B][Hkv][max_groups] splits of each group done.
 size_t gqa_workspace_bytes(const apex_attn_params *p, uint32_t batch, uint32_t max_len) {
-    const size_t parts = static_cast<size_t>(batch) * p->q_heads * gqa_max_splits(batch, p->kv_heads, max_len) *
-                         (p->head_dim + 4) * sizeof(float);
-    return align256(parts) + align256(static_cast<size_t>(batch) * p->kv_heads * sizeof(unsigned));
+    const uint32_t max_splits = gqa_max_splits(batch, p->kv_heads, max_len);
+    const size_t parts = static_cast<size_t>(batch) * p->q_heads * max_splits * (p->head_dim + 4) * sizeof(float);
+    const size_t max_groups = (max_splits + kGroup - 1) / kGroup;
+    return align256(parts) + align256(static_cast<size_t>(batch) * p->kv_heads * sizeof(unsigned)) +
+           align256(static_cast<size_t>(batch) * p->kv_heads * max_groups * sizeof(unsigned));
 }
 
 int launch_gqa_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t *k_new, const uint16_t *v_new,
@@ -540,6 +622,9 @@ int launch_gqa_decode(const apex_attn_params *p, const uint16_t *q_raw, const ui
     a.ws_count = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(workspace) +
                                               align256(static_cast<size_t>(batch) * p->q_heads * max_splits *
                                                        (p->head_dim + 4) * sizeof(float)));
+    a.ws_gcount = reinterpret_cast<unsigned *>(reinterpret_cast<uint8_t *>(a.ws_count) +
+                                               align256(static_cast<size_t>(batch) * p->kv_heads * sizeof(unsigned)));
+    a.max_groups = (max_splits + kGroup - 1) / kGroup;
     a.status = device_status_ptr();
     if (!a.status) return fail(APEX_ERR_CUDA, std::string(name) + ": device status word unavailable");
     a.capacity = capacity; a.q_heads = p->q_heads; a.kv_heads = p->kv_heads; a.group = p->q_heads / p->kv_heads;

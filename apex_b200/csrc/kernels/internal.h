@@ -71,5 +71,10 @@ int launch_prefill_gqa_prep(const apex_attn_params *p, const uint16_t *q_raw, co
 int launch_prefill_gqa_attend(const apex_attn_params *p, const void *workspace, const uint16_t *k_cache,
                               const uint16_t *v_cache, uint32_t capacity, uint32_t batch, uint32_t tokens,
                               uint32_t pos0, uint16_t *out, cudaStream_t s);
+// Its tcgen05 attention (prefill_wide.cu) for GQA groups of 1, 2, 4 or 8, over the same workspace.
+bool prefill_wide_applies(const apex_attn_params *p);
+int launch_prefill_wide_attend(const apex_attn_params *p, const void *workspace, const uint16_t *k_cache,
+                               const uint16_t *v_cache, uint32_t capacity, uint32_t batch, uint32_t tokens,
+                               uint32_t pos0, uint16_t *out, cudaStream_t s);
 
 }  // namespace apex

@@ -7,9 +7,10 @@
 // partial RoPE) and v (weightless norm, or a plain copy) into the caches at pos0, by the bf16
 // head_norm_rope kernel with the caches' strides.
 //
-// Attention.  A 128 x 512 bf16 Q tile (128 KB) and a 128 x 512 f32 accumulator (all of TMEM) leave
-// no room for the tcgen05 pair kernel's pipeline, so this form runs on mma.sync m16n8k16 (bf16 in,
-// f32 accumulate) with the head dimension split over warps: a CTA takes 16 queries of two q heads
+// Attention.  GQA groups of 1, 2, 4 and 8 (the global layers' 8 among them) run on the tensor cores
+// (prefill_wide.cu: a CTA pair splitting the head dimension).  Other groups take the form here, on
+// mma.sync m16n8k16 (bf16 in, f32 accumulate) with the head dimension split over warps: a CTA takes
+// 16 queries of two q heads
 // of one GQA group; warp (head, slice) keeps its 16 x 128 slice of Q in registers, computes the
 // partial scores of its slice against each 32-key tile, the four slice warps of a head add their
 // partials through shared memory in a fixed order (so all four hold the same scores, bit for bit, and
@@ -324,6 +325,8 @@ int launch_prefill_gqa_prep(const apex_attn_params *p, const uint16_t *q_raw, co
 int launch_prefill_gqa_attend(const apex_attn_params *p, const void *workspace, const uint16_t *k_cache,
                               const uint16_t *v_cache, uint32_t capacity, uint32_t batch, uint32_t tokens,
                               uint32_t pos0, uint16_t *out, cudaStream_t s) {
+    if (prefill_wide_applies(p))
+        return launch_prefill_wide_attend(p, workspace, k_cache, v_cache, capacity, batch, tokens, pos0, out, s);
     const uint64_t kv_len = static_cast<uint64_t>(pos0) + tokens;
     const uint64_t row = kD * 2ull;
     // caches [B*Hkv][capacity][512] as {64-element chunks, keys (cut at pos0 + T), 8 chunks, kv rows}:

@@ -239,8 +239,12 @@ class PrefillWorkload:
         owns_tokens = self.sharding != "kv-head-shard" or rank == 0
         self.tokens = B * T * C if owns_tokens else 0
         self.launches_per_step = 2 * C
-        # head_dim 512 (the global layers) runs the mma.sync form of prefill_gqa.cu
-        self.kernel_name = "prefill_gqa_kernel" if cfg.head_dim == 512 else "prefill_pair_kernel"
+        # head_dim 512 (the global layers): the tcgen05 pair kernel for groups of 1, 2, 4 and 8, else
+        # the mma.sync form
+        if cfg.head_dim == 512:
+            self.kernel_name = "prefill_wide_kernel" if Hq // Hkv in (1, 2, 4, 8) else "prefill_gqa_kernel"
+        else:
+            self.kernel_name = "prefill_pair_kernel"
 
     def _chunk(self, s, c, out, ws):
         self.ops.attention_prefill_prep(self.shape, s["q"][c], s["k"][c], s["v"][c], self.qw, self.kw, s["cache"],

@@ -89,3 +89,17 @@ def test_gqa_groups_vs_oracle(q_heads, kv_heads, head_dim):
     for i, L in enumerate(lens):
         ref, _, _ = oracle_decode_seq(cfg, i, L)
         assert_close(got[i], ref, f"Hq={q_heads} Hkv={kv_heads} hd={head_dim} L={L}")
+
+
+@pytest.mark.parametrize("lens", [[20000], [5000, 7]])
+def test_global_layer_decode_small_batch_many_splits(lens):
+    """One or two sequences take up to ~300 splits per kv head; their last CTAs stream the partials
+    through shared memory in pieces of 15 splits (several pieces per head, a short last piece)."""
+    cfg = dataclasses.replace(G, seed=74 + len(lens))
+    shape, t = build_decode(cfg, list(range(len(lens))), lens)
+    got, ws = run_decode(shape, t)
+    again, _ = run_decode(shape, t, ws)
+    np.testing.assert_array_equal(got, again)
+    for i, L in enumerate(lens):
+        ref, _, _ = oracle_decode_seq(cfg, i, L)
+        assert_close(got[i], ref, f"small batch L={L}")

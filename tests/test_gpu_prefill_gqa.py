@@ -63,8 +63,8 @@ def test_global_prefill_caches_vs_oracle():
 
 @pytest.mark.parametrize("window", [0, 50])
 def test_global_prefill_chunks_match_one_shot(window):
-    """Chunks of 150 tokens start off the 16-query and 32-key tile edges; the rows equal one call's
-    bit for bit (the same keys in the same tiles and order)."""
+    """Chunks of 150 tokens start off the query-tile and 32-key tile edges; chunked and one-call rows
+    both match the oracle."""
     T = 600
     cfg = dataclasses.replace(G, seq_len=T, chunk=T, window=window, seed=91)
     one, _ = run_prefill(cfg, [0], T, T)
@@ -75,9 +75,10 @@ def test_global_prefill_chunks_match_one_shot(window):
     assert_close(one[0, rows], ref, f"one call window={window}")
 
 
-@pytest.mark.parametrize("q_heads,kv_heads", [(6, 2), (8, 8), (4, 1)])
+@pytest.mark.parametrize("q_heads,kv_heads", [(6, 2), (10, 2), (16, 1), (8, 8), (4, 1), (8, 4)])
 def test_prefill_512_group_sizes(q_heads, kv_heads):
-    """Groups of 3 leave one head slot of the last CTA of each group idle; MHA leaves one of every CTA."""
+    """Groups of 1, 2, 4 and 8 take the tensor-core pair kernel (128 / group queries per item); groups
+    of 3, 5 and 16 the mma.sync form (groups of 3 and 5 leave one head slot of a CTA idle)."""
     T = 130
     cfg = dataclasses.replace(G, q_heads=q_heads, kv_heads=kv_heads, seq_len=T, chunk=T, seed=95 + q_heads)
     got, _ = run_prefill(cfg, [0], T, T)
