@@ -111,11 +111,19 @@ using DecodeSmem = DecodeSmemT<kConsumerWarps, kStages, false>;
 __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+// Relaxed system-scope flag accesses: ordered by one fence on each side (release: a fence before the
+// flag stores; acquire: a fence after the flag loads), not by one fence per flag.  Each release
+// store is a system-scope fence of its own, which waits for this thread's earlier stores to every
+// peer to be acknowledged over NVLink: one per peer made the publish cost grow with the rank count.
+__device__ __forceinline__ void st_relaxed_sys(unsigned *p, unsigned v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned *p) {
     unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 template <int CW = kConsumerWarps>
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
@@ -288,13 +296,13 @@ __device__ void peer_publish_merge(const DecodeArgs &a, DecodeSmem &sm, uint32_t
     if (tid == 0) {
         a.peer_seq[bkv] = seq;
         __threadfence_system();  // every thread's stores above (ordered by the barrier) before the flags
-        for (uint32_t p = 0; p < a.world; ++p) st_release_sys(a.peer_flags[p] + a.rank * bhkv + bkv, seq);
+        for (uint32_t p = 0; p < a.world; ++p) st_relaxed_sys(a.peer_flags[p] + a.rank * bhkv + bkv, seq);
         const unsigned *mine = a.peer_flags[a.rank] + bkv;
         const unsigned long long start = globaltimer_ns();
         bool ok = true;
         for (uint32_t r = 0; r < a.world && ok; ++r) {
             for (;;) {
-                const unsigned f = ld_acquire_sys(mine + r * bhkv);
+                const unsigned f = ld_relaxed_sys(mine + r * bhkv);
                 if (f & kPeerPoison) {  // that rank gave up on this pair
                     ok = false;
                     break;
@@ -307,6 +315,7 @@ __device__ void peer_publish_merge(const DecodeArgs &a, DecodeSmem &sm, uint32_t
                 __nanosleep(64);
             }
         }
+        fence_acq_rel_sys();  // the flags seen above before the peers' partials are read
         if (!ok) {
             atomicOr(a.status, kStatusTimeout);
             a.peer_seq[bkv] = seq | kPeerPoison;
@@ -791,6 +800,36 @@ uint32_t choose_chunk(uint32_t batch, uint32_t kv_heads, uint32_t range_len) {
     return static_cast<uint32_t>(std::min<uint64_t>(std::max<uint64_t>(c, kStagePos), 1u << 24));
 }
 
+// Splits of a KV split's partial modes, where every sequence covers the same key range (each rank
+// holds the same positions of every sequence), so a plan launches exactly batch * kv_heads * splits
+// CTAs.  The split size is the one with the least modelled time -- whole waves of two CTAs per SM,
+// each as long as a split plus a fixed per-CTA cost -- among sizes of at least the floor above
+// (ties keep the larger split).  A last wave that is half empty costs as much as a full one: at 8
+// GPUs a batch of 8 sequences of 131072 keys gives each rank 16384 keys per sequence, which
+// 1024-key splits cut into 3.46 waves; 9 splits per (sequence, kv head) fill two.
+constexpr uint64_t kCtaCostPos = 64;  // per-CTA set-up and merge, in key positions of streaming
+
+uint32_t choose_chunk_equal(uint32_t batch, uint32_t kv_heads, uint32_t range_len) {
+    const uint64_t pairs = static_cast<uint64_t>(batch) * kv_heads;
+    const uint64_t len = std::max<uint32_t>(range_len, 1);
+    const uint64_t one_wave = 2ull * static_cast<uint64_t>(sm_count());
+    const uint64_t wave_chunk = (pairs * len + one_wave - 1) / one_wave;
+    const uint64_t floor_c = batch == 1 ? wave_chunk : std::min<uint64_t>(wave_chunk, kMinChunkPos);
+    uint64_t best_c = 0, best_cost = ~0ull;
+    for (uint64_t s = 1; s <= len; ++s) {
+        const uint64_t c = ((len + s - 1) / s + kStagePos - 1) / kStagePos * kStagePos;
+        if (c < floor_c) break;
+        const uint64_t ctas = pairs * ((len + c - 1) / c);
+        const uint64_t cost = (ctas + one_wave - 1) / one_wave * (c + kCtaCostPos);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best_c = c;
+        }
+    }
+    if (!best_c || best_c > (1u << 24)) return choose_chunk(batch, kv_heads, range_len);
+    return static_cast<uint32_t>(best_c);
+}
+
 uint32_t max_splits_for(uint32_t batch, uint32_t kv_heads, uint32_t max_len) {
     const uint64_t by_len = (static_cast<uint64_t>(max_len) + kStagePos - 1) / kStagePos;
     const uint64_t by_target = target_ctas() / std::max<uint64_t>(1, static_cast<uint64_t>(batch) * kv_heads) + 2;
@@ -967,7 +1006,8 @@ int plan_decode(const apex_attn_params *p, const uint16_t *q_raw, const uint16_t
         align256(static_cast<size_t>(batch) * p->q_heads * max_splits * kWsRec * sizeof(float)));
     a.capacity = capacity; a.q_heads = p->q_heads; a.kv_heads = p->kv_heads;
     a.rope_pairs = p->rope_pairs; a.window = p->window; a.qk_norm = p->qk_norm; a.v_norm = p->v_norm;
-    a.chunk = choose_chunk(batch, p->kv_heads, range_len);
+    a.chunk = partial_mode ? choose_chunk_equal(batch, p->kv_heads, range_len)
+                           : choose_chunk(batch, p->kv_heads, range_len);
     a.max_splits = max_splits;
     a.kv_begin = kv_begin; a.kv_end = kv_end; a.max_seq_len = max_seq_len;
     a.ring = ring ? 1u : 0u;

@@ -64,7 +64,7 @@ L2_BYTES = 126 * 1024 * 1024
 TOL_MAX, TOL_MEAN = 2e-2, 2e-3          # against an fp32 reference
 TOL_SPLIT_MAX, TOL_SPLIT_MEAN = 4e-3, 2e-4  # KV split vs the one-GPU decode (same bf16 inputs)
 # DRAM bytes (read + write) per launch of the dominant kernel from one ncu capture of that
-# workload (the profiles/ summaries name the commands); None where no capture exists.  The 8.6 GB
+# workload; None where no capture exists.  The 8.6 GB
 # c5_long_decode_b8 is too large to capture under the size rule: its figure is the c5_long_decode_b1
 # capture (same kernel, same keys per sequence) times the 8 sequences -- the traffic is per-sequence
 # K/V streaming and grows in proportion.
@@ -594,20 +594,33 @@ class ProjWorkload:
             sc = torch.where((b & 0x80) != 0, -sc, sc)
             return lut[nib] * sc.repeat_interleave(16, 1)
 
-        worst, rel = 0.0, 0.0
+        worst, rel, over = 0.0, 0.0, 0.0
         for name, out in (("q", self.q), ("k", self.k), ("v", self.v)):
-            ref = (dense(W[name]) @ self.x.double().T).T
+            Wd = dense(W[name])
+            ref = (Wd @ self.x.double().T).T
             if self.prefill:  # millions of outputs, some near zero: the bf16 rounding as a relative L2
                 err = ((out.double() - ref).norm() / ref.norm()).item()
             else:
-                err = ((out.double() - ref).abs() / ref.abs().clamp_min(1e-3)).max().item()
+                # one bf16 rounding of each output (2^-9 of |ref|, doubled) plus the f32 accumulation
+                # error, bounded by 1e-6 of sum |w x| (outputs that nearly cancel have a large
+                # relative error that is neither rounding nor a fault)
+                absdot = (Wd.abs() @ self.x.double().abs().T).T
+                diff = (out.double() - ref).abs()
+                err = (diff / ref.abs().clamp_min(1e-3)).max().item()
+                over = max(over, (diff / (2 ** -8 * ref.abs() + 1e-6 * absdot)).max().item())
             worst = max(worst, err)
         ro = (dense(W["o"]) @ self.att.double().T).T
         ro = ro * torch.rsqrt((ro ** 2).mean(-1, keepdim=True) + 1e-6) * self.nw.double()
         rel = ((self.o.double() - ro).norm() / ro.norm()).item()
         key = "qkv_bf16_rel_l2" if self.prefill else "qkv_bf16_max_rel"
-        return {"max_abs": worst, "mean_abs": rel, "o_proj_norm_rel_l2": rel, key: worst,
-                "ref": "torch fp64: weights decoded from the E2M1 / E4M3 bits", "ok": rel < 1e-5 and worst <= 2 ** -8}
+        rep = {"max_abs": worst, "mean_abs": rel, "o_proj_norm_rel_l2": rel, key: worst,
+               "ref": "torch fp64: weights decoded from the E2M1 / E4M3 bits"}
+        if self.prefill:
+            rep["ok"] = rel < 1e-5 and worst <= 2 ** -8
+        else:
+            rep["qkv_err_over_bound"] = over  # bound: 2^-8 |ref| + 1e-6 sum |w x|
+            rep["ok"] = rel < 1e-5 and over <= 1.0
+        return rep
 
     def close(self):
         pass
