@@ -40,7 +40,6 @@ constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStagePos = kConsumerWarps * kPosPerWarp;
 constexpr int kStages = 3;
-constexpr int kStageBytes = kStagePos * kRowBytes;
 // Cluster form (short contexts): 8 consumer warps, stages of 64 positions, a 1- or 2-stage ring; the
 // splits of one (sequence, kv head) form one thread-block cluster and merge in the leader CTA's
 // shared memory.
@@ -50,6 +49,7 @@ constexpr uint32_t kMaxCluster = 16;
 constexpr uint32_t kShortMaxLen = 4096;  // longest context the cluster form is chosen for
 constexpr int kPart = kD + 2;           // public partial record: o[D], m, l
 constexpr int kWsRec = kD + 4;          // workspace record: o[D], m, l, pad (16-byte multiple)
+constexpr int kLLRec = kD + 2;          // peer gather record: o[D], m, l as 8-byte (step, value) words
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kMaxPeers = 8;       // GPUs of one NVLink domain that share a KV range
 
@@ -72,7 +72,7 @@ struct DecodeArgs {
     // all partials itself once every rank's flag has arrived (no collective launch, no merge launch)
     int peer_mode;
     uint32_t rank, world;
-    float *peer_gather[kMaxPeers];    // rank r's [2 step parity][world][B*Hq][D+4] f32, mapped here
+    float *peer_gather[kMaxPeers];    // rank r's [2 step parity][world][B*Hq][D+2] (step, f32) words, mapped here
     unsigned *peer_flags[kMaxPeers];  // rank r's [world][B*Hkv] last published step
     unsigned *peer_seq;               // this rank's [B*Hkv] step counters
     unsigned long long peer_wait_ns;  // bound of the wait for the other ranks' flags
@@ -111,19 +111,12 @@ using DecodeSmem = DecodeSmemT<kConsumerWarps, kStages, false>;
 __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Relaxed system-scope flag accesses: ordered by one fence on each side (release: a fence before the
-// flag stores; acquire: a fence after the flag loads), not by one fence per flag.  Each release
-// store is a system-scope fence of its own, which waits for this thread's earlier stores to every
-// peer to be acknowledged over NVLink: one per peer made the publish cost grow with the rank count.
-__device__ __forceinline__ void st_relaxed_sys(unsigned *p, unsigned v) {
-    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
+// Relaxed system-scope access to the poison flags (the data words carry their own step number).
 __device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned *p) {
     unsigned v;
     asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 template <int CW = kConsumerWarps>
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
@@ -265,13 +258,29 @@ __device__ __forceinline__ void consumer_reduce(float (&v)[kG], float (&red)[CW]
 
 // Peer mode: publish this rank's partial of (b, kv head) -- thread t holds head g = t / 64, dims
 // [d0, d0+4) of the normalised o, and (m, l) when d0 = 0 -- to every rank, then merge all ranks'
-// partials into bf16 out.  Steps alternate between two gather slots, so a rank that runs ahead never
-// overwrites data a slower peer is still merging (it cannot start step k+2 before every peer has
-// published step k+1, which each peer does only after finishing step k).  The wait for the peers'
-// flags is bounded (a.peer_wait_ns): on expiry, or when a peer's flag is poisoned, the status word
-// gets kStatusTimeout, the output is left unwritten, and this pair's counter and this rank's flag on
-// every peer are poisoned, so that no rank publishes into or merges from the gather slots again (the
-// ordering above assumed a wait that succeeded).
+// partials into bf16 out.  Every value travels as one 8-byte word (step << 32 | float bits) written
+// with 16-byte stores of two words; an aligned 8-byte word is written and read as a whole, so a
+// reader that polls its own words until their step matches this step has the data without any
+// flag or fence (a system-scope fence per published partial, which waits for the NVLink stores to
+// be acknowledged, cost more than the wait itself).  Steps alternate between two gather slots, so a
+// rank that runs ahead never overwrites data a slower peer is still merging (it cannot start step
+// k+2 before it has read every peer's step k+1, which each peer publishes only after finishing step
+// k).  The wait is bounded (a.peer_wait_ns): on expiry, or when a peer's poison flag is set, the
+// status word gets kStatusTimeout, the output is left unwritten, and this pair's counter and this
+// rank's poison flag on every peer are set, so that no rank publishes into or merges from the
+// gather slots again (the ordering above assumed a wait that succeeded).
+__device__ __forceinline__ void st_sys_v2(uint64_t *p, uint64_t x, uint64_t y) {
+    asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(x), "l"(y) : "memory");
+}
+__device__ __forceinline__ void ld_sys_v2(const uint64_t *p, uint64_t &x, uint64_t &y) {
+    asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(p) : "memory");
+}
+__device__ __forceinline__ uint64_t ll_word(unsigned seq, float v) {
+    return (static_cast<uint64_t>(seq) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ float ll_value(uint64_t w) { return __uint_as_float(static_cast<unsigned>(w)); }
+__device__ __forceinline__ bool ll_is(uint64_t w, unsigned seq) { return static_cast<unsigned>(w >> 32) == seq; }
+
 __device__ void peer_publish_merge(const DecodeArgs &a, DecodeSmem &sm, uint32_t b, uint32_t kvh, uint32_t tid,
                                    uint32_t g, uint32_t d0, const float (&o)[4], float m, float l) {
     const uint32_t bhkv = gridDim.z * a.kv_heads, bkv = b * a.kv_heads + kvh;
@@ -285,66 +294,76 @@ __device__ void peer_publish_merge(const DecodeArgs &a, DecodeSmem &sm, uint32_t
     const unsigned seq = prev + 1u;
     const uint32_t par = seq & 1u;
     for (uint32_t p = 0; p < a.world; ++p) {
-        float *dst = a.peer_gather[p] + ((static_cast<uint64_t>(par) * a.world + a.rank) * rows + row) * kWsRec;
-        *reinterpret_cast<float4 *>(dst + d0) = make_float4(o[0], o[1], o[2], o[3]);
-        if (d0 == 0) {
-            dst[kD] = m;
-            dst[kD + 1] = l;
+        uint64_t *dst = reinterpret_cast<uint64_t *>(a.peer_gather[p]) +
+                        ((static_cast<uint64_t>(par) * a.world + a.rank) * rows + row) * kLLRec;
+        st_sys_v2(dst + d0, ll_word(seq, o[0]), ll_word(seq, o[1]));
+        st_sys_v2(dst + d0 + 2, ll_word(seq, o[2]), ll_word(seq, o[3]));
+        if (d0 == 0) st_sys_v2(dst + kD, ll_word(seq, m), ll_word(seq, l));
+    }
+    // every thread waits for its own words (and the head's m, l) of every rank
+    const uint64_t *base = reinterpret_cast<const uint64_t *>(a.peer_gather[a.rank]) +
+                           static_cast<uint64_t>(par) * a.world * rows * kLLRec;
+    float ov[kMaxPeers][4], mr[kMaxPeers], lr[kMaxPeers];
+    bool ok = true;
+    const unsigned long long start = globaltimer_ns();
+#pragma unroll
+    for (uint32_t r = 0; r < kMaxPeers; ++r) {
+        mr[r] = -INFINITY;
+        lr[r] = 0.f;
+        if (r >= a.world || !ok) continue;
+        const uint64_t *src = base + (r * rows + row) * kLLRec;
+        for (;;) {
+            uint64_t w0, w1, w2, w3, w4, w5;
+            ld_sys_v2(src + d0, w0, w1);
+            ld_sys_v2(src + d0 + 2, w2, w3);
+            ld_sys_v2(src + kD, w4, w5);
+            if (ll_is(w0, seq) && ll_is(w1, seq) && ll_is(w2, seq) && ll_is(w3, seq) && ll_is(w4, seq) &&
+                ll_is(w5, seq)) {
+                ov[r][0] = ll_value(w0);
+                ov[r][1] = ll_value(w1);
+                ov[r][2] = ll_value(w2);
+                ov[r][3] = ll_value(w3);
+                mr[r] = ll_value(w4);
+                lr[r] = ll_value(w5);
+                break;
+            }
+            if ((ld_relaxed_sys(a.peer_flags[a.rank] + r * bhkv + bkv) & kPeerPoison) ||  // that rank gave up
+                globaltimer_ns() - start > a.peer_wait_ns) {
+                ok = false;
+                break;
+            }
+            __nanosleep(32);
         }
     }
+    if (tid == 0) sm.is_last = 1;
     consumer_sync();
-    if (tid == 0) {
-        a.peer_seq[bkv] = seq;
-        __threadfence_system();  // every thread's stores above (ordered by the barrier) before the flags
-        for (uint32_t p = 0; p < a.world; ++p) st_relaxed_sys(a.peer_flags[p] + a.rank * bhkv + bkv, seq);
-        const unsigned *mine = a.peer_flags[a.rank] + bkv;
-        const unsigned long long start = globaltimer_ns();
-        bool ok = true;
-        for (uint32_t r = 0; r < a.world && ok; ++r) {
-            for (;;) {
-                const unsigned f = ld_relaxed_sys(mine + r * bhkv);
-                if (f & kPeerPoison) {  // that rank gave up on this pair
-                    ok = false;
-                    break;
-                }
-                if (static_cast<int>(f - seq) >= 0) break;
-                if (globaltimer_ns() - start > a.peer_wait_ns) {
-                    ok = false;
-                    break;
-                }
-                __nanosleep(64);
-            }
-        }
-        fence_acq_rel_sys();  // the flags seen above before the peers' partials are read
-        if (!ok) {
+    if (!ok) sm.is_last = 0;
+    consumer_sync();
+    if (!sm.is_last) {
+        if (tid == 0) {
             atomicOr(a.status, kStatusTimeout);
             a.peer_seq[bkv] = seq | kPeerPoison;
             for (uint32_t p = 0; p < a.world; ++p)
                 st_release_sys(a.peer_flags[p] + a.rank * bhkv + bkv, seq | kPeerPoison);
         }
-        sm.is_last = ok;
+        return;
     }
-    consumer_sync();
-    if (!sm.is_last) return;
+    if (tid == 0) a.peer_seq[bkv] = seq;
     // log-sum-exp merge over the ranks (each partial: o normalised by its l, l relative to its m)
-    const float *base = a.peer_gather[a.rank] + static_cast<uint64_t>(par) * a.world * rows * kWsRec;
     float M = -INFINITY;
-    for (uint32_t r = 0; r < a.world; ++r) {
-        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(base + (r * rows + row) * kWsRec + kD));
-        if (ml.y > 0.f) M = fmaxf(M, ml.x);
-    }
+#pragma unroll
+    for (uint32_t r = 0; r < kMaxPeers; ++r)
+        if (lr[r] > 0.f) M = fmaxf(M, mr[r]);
     float den = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (uint32_t r = 0; r < a.world; ++r) {
-        const float *src = base + (r * rows + row) * kWsRec;
-        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(src + kD));
-        if (!(ml.y > 0.f)) continue;
-        const float wt = fast_exp2(ml.x - M) * ml.y;
-        const float4 ov = __ldcg(reinterpret_cast<const float4 *>(src + d0));
+#pragma unroll
+    for (uint32_t r = 0; r < kMaxPeers; ++r) {
+        if (!(lr[r] > 0.f)) continue;
+        const float wt = fast_exp2(mr[r] - M) * lr[r];
         den += wt;
-        acc[0] += wt * ov.x;
-        acc[1] += wt * ov.y;
-        acc[2] += wt * ov.z;
-        acc[3] += wt * ov.w;
+        acc[0] += wt * ov[r][0];
+        acc[1] += wt * ov[r][1];
+        acc[2] += wt * ov[r][2];
+        acc[3] += wt * ov[r][3];
     }
     const float inv = den > 0.f ? 1.0f / den : 0.f;
     uint2 packed;
@@ -1156,7 +1175,7 @@ extern "C" int apex_attn_peer_exchange_bytes(const apex_attn_params *p, uint32_t
         return fail(APEX_ERR_INVALID_ARGUMENT, "apex_attn_peer_exchange_bytes: need 1 <= world <= 8");
     if (!gather_bytes || !flag_bytes || !seq_bytes)
         return fail(APEX_ERR_INVALID_ARGUMENT, "apex_attn_peer_exchange_bytes: null output");
-    *gather_bytes = 2ull * world * batch * p->q_heads * kWsRec * sizeof(float);  // 16-byte records
+    *gather_bytes = 2ull * world * batch * p->q_heads * kLLRec * sizeof(uint64_t);  // 16-byte multiples
     *flag_bytes = static_cast<size_t>(world) * batch * p->kv_heads * sizeof(uint32_t);
     *seq_bytes = static_cast<size_t>(batch) * p->kv_heads * sizeof(uint32_t);
     return ok();

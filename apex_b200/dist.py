@@ -9,8 +9,8 @@ Only these shardings exist, where the work splits naturally:
 * KV-sequence split (one long decode): rank r holds key positions [begin_r, end_r) of every
   sequence.  Fused form (PeerExchangeBuffers + apex_attn_decode_kvsplit_bf16): the decode
   kernel writes each rank's partial (o, m, l) straight into every rank's gather buffer over
-  NVLink (CUDA IPC mappings), raises a per-step flag there and merges once all flags are in --
-  one launch per step.  Collective form (KVSplitDecode, the baseline): the partial from
+  NVLink (CUDA IPC mappings), each value as an 8-byte word carrying the step number, and merges
+  once every rank's words carry the step -- one launch per step.  Collective form (KVSplitDecode, the baseline): the partial from
   apex_attn_decode_partial_bf16, ONE NCCL all-gather (16.5 KB per sequence per rank at Hq=16,
   D=256) and apex_attn_merge_partials.
 

@@ -191,18 +191,20 @@ APEX_API int apex_attn_decode_partial_bf16(const apex_attn_params *p, const uint
  * The reference runs on one device, so nothing here has a counterpart in it.  A KV range split
  * over the GPUs of one NVLink domain is merged inside the decode kernel: each rank writes its
  * partial (the apex_attn_decode_partial_bf16 record) straight into every rank's gather buffer
- * over NVLink, raises a per-step flag there, waits for every rank's flag (bounded: on expiry the
- * device status word reports a timeout) and merges.  One launch per step, no collective call.
+ * over NVLink, each value as one 8-byte word that carries the step number beside it, waits until
+ * its words of every rank carry this step (bounded: on expiry the device status word reports a
+ * timeout) and merges.  One launch per step, no collective call, no flag and no fence.
  *
  * Buffers (per rank, zero-initialised, e.g. by apex_device_alloc; shared with the other ranks by
  * apex_ipc_get_handle / apex_ipc_open_handle):
- *   gather  [2][world][batch*q_heads][head_dim+4] f32   (two slots, alternating by step)
- *   flags   [world][batch*kv_heads] uint32               (last step each rank published)
+ *   gather  [2][world][batch*q_heads][head_dim+2] uint64 (step << 32 | f32 bits; two slots,
+ *                                                         alternating by step)
+ *   flags   [world][batch*kv_heads] uint32               (a rank's poison mark, set on failure)
  *   seq     [batch*kv_heads] uint32                      (this rank's step counters)
  * Every rank must call apex_attn_decode_kvsplit_bf16 the same number of times with the same
  * batch and the same world; calls on one rank are serialised (one stream).
  *
- * Failure: the wait for the other ranks' flags gives up after wait_ns (0 = one second).  The
+ * Failure: the wait for the other ranks' partials gives up after wait_ns (0 = one second).  The
  * step then leaves `out` unwritten for that (sequence, kv head), the device status word reports
  * a timeout (apex_cuda_device_status returns APEX_ERR_DEVICE_TIMEOUT), and the pair's step counter
  * and this rank's flag on every peer are poisoned: every later step of that pair, on every rank,
