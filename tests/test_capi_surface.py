@@ -58,6 +58,22 @@ def test_workspace_sizes_are_host_computable():
     assert 0 < small < big
 
 
+def test_peer_exchange_sizes_follow_the_documented_layout():
+    """gather [2][world][batch*q_heads][head_dim+2] 8-byte (step, value) words, flags
+    [world][batch*kv_heads] and seq [batch*kv_heads] uint32; at most 8 ranks."""
+    lib = _native.load()
+    p = _params()
+    sizes = [ctypes.c_size_t() for _ in range(3)]
+    for batch, world in ((1, 1), (8, 2), (8, 8)):
+        _native.check(lib.apex_attn_peer_exchange_bytes(ctypes.byref(p), batch, world, *map(ctypes.byref, sizes)))
+        gather, flags, seq = (s.value for s in sizes)
+        assert gather == 2 * world * batch * 16 * (256 + 2) * 8
+        assert flags == world * batch * 8 * 4 and seq == batch * 8 * 4
+        assert gather % 16 == 0  # every record starts on a 16-byte boundary (16-byte stores)
+    assert lib.apex_attn_peer_exchange_bytes(ctypes.byref(p), 1, 9, *map(ctypes.byref, sizes)) == \
+        _native.APEX_ERR_INVALID_ARGUMENT
+
+
 @pytest.mark.parametrize("kw,code", [(dict(head_dim=128), _native.APEX_ERR_UNSUPPORTED),
                                      (dict(q_heads=12, kv_heads=8), _native.APEX_ERR_INVALID_ARGUMENT),
                                      (dict(rope_pairs=200), _native.APEX_ERR_INVALID_ARGUMENT),
