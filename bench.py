@@ -75,6 +75,7 @@ NCU_TRAFFIC_BYTES = {
     "c5_long_decode_b1": _C5_B1_TRAFFIC,
     "c5_long_decode_b8": 8 * _C5_B1_TRAFFIC,
     "global_decode": 1_074_024_000 + 4_393_472,
+    "global_prefill": 83_921_920 + 26_314_496,
 }
 
 
